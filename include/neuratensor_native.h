@@ -1,0 +1,174 @@
+/*
+ * neuratensor_native.h -- C ABI of libneuratensor_native.so
+ *
+ * B200 (sm_100a) kernels for the FusedSpikeBlock inference path of
+ * NeuraTensor 4.0.4.  Every entry point takes plain device pointers, sizes
+ * and element strides, runs asynchronously on the given CUDA stream and
+ * returns an nt_status code; it never aborts the process.  The caller owns
+ * every buffer: inputs, outputs, state buffers and workspaces (sized with
+ * the *_workspace_bytes queries).  The library keeps no per-call state, so
+ * calls on different streams may run concurrently.
+ *
+ * Reference interfaces replaced (paths inside the NeuraTensor source tree):
+ *   nt_lif_scan            LIFLayer.forward            neuratensor/core/snn.py:264-312
+ *                          (_lif_sequential_scan :167-182, _lif_single_step :64-75)
+ *   nt_selective_scan      SelectiveSSMLayer._discretize + _scan_sequential / _scan_single_step
+ *                                                      neuratensor/core/ssm.py:106-139,145-221
+ *   nt_ssm_forward         SelectiveSSMLayer.forward   neuratensor/core/ssm.py:313-349
+ *   nt_sparse_out_proj     FusedSpikeBlock._sparse_out_proj  neuratensor/core/fused.py:149-165
+ *   nt_rmsnorm_in_proj     FusedSpikeBlock.norm + in_proj    neuratensor/core/fused.py:118-119
+ *   nt_block_forward       FusedSpikeBlock.forward     neuratensor/core/fused.py:101-147
+ *   nt_lif_ssm_fused       LIF spikes driving the selective scan with given dt/B/C
+ *                          (snn.py:167-182 feeding ssm.py:106-139,184-221)
+ *
+ * Layouts: activations are row-major [rows, channels] with unit channel
+ * stride; "rows" are (batch, time) pairs in batch-major order.  Weights are
+ * the nn.Linear weights, row-major [out_features, in_features].
+ */
+#ifndef NEURATENSOR_NATIVE_H
+#define NEURATENSOR_NATIVE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NT_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define NT_API __attribute__((visibility("default")))
+#else
+#define NT_API
+#endif
+
+typedef enum {
+    NT_F32 = 0,   /* float32                                   */
+    NT_BF16 = 1,  /* bfloat16                                  */
+    NT_U8 = 2     /* uint8 (spike output of nt_lif_ssm_fused)  */
+} nt_dtype;
+
+typedef enum {
+    NT_OK = 0,
+    NT_ERR_ARG = 1,        /* bad shape, stride, null pointer or alignment          */
+    NT_ERR_DTYPE = 2,      /* unsupported dtype combination                          */
+    NT_ERR_ARCH = 3,       /* device is not sm_100                                   */
+    NT_ERR_CUDA = 4,       /* CUDA runtime / launch error                            */
+    NT_ERR_TIMEOUT = 5,    /* a bounded device-side wait expired (see error flag)    */
+    NT_ERR_WORKSPACE = 6   /* workspace pointer null or smaller than required        */
+} nt_status;
+
+/* Library / device queries ------------------------------------------------ */
+NT_API int nt_abi_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+NT_API const char* nt_last_error(void);
+/* NT_OK when `device` is an sm_100 GPU this build can run on. */
+NT_API int nt_device_supported(int device);
+/* Reads (and optionally clears) the device error word that kernels set when
+ * a bounded wait expires.  Synchronises the device.  *flags == 0 means no
+ * kernel reported an error. */
+NT_API int nt_get_error_flag(int device, unsigned* flags, int clear);
+
+/* (a) LIF membrane recurrence -- LIFLayer.forward (snn.py:264-312).
+ * Per channel c and step t:  V = beta[c]*V + x[t,c]  (a product then a sum,
+ * each rounded to `dtype`), S = (V >= threshold[c]), V = V - threshold[c]*S.
+ * x: [B,T,C] with element strides (x_sb, x_st, 1); spikes written as 0/1 in
+ * `dtype` with strides (s_sb, s_st, 1).  beta, threshold: [C] in `dtype`.
+ * mem_in: [B,C] in `dtype` or NULL for zeros (snn.py:286-287); mem_out: [B,C].
+ * spike_count: optional device uint64 that is incremented by the number of
+ * spikes (caller zeroes it). */
+NT_API int nt_lif_scan(int dtype, int64_t B, int64_t T, int64_t C,
+                const void* x, int64_t x_sb, int64_t x_st,
+                const void* beta, const void* threshold,
+                const void* mem_in, void* mem_out,
+                void* spikes, int64_t s_sb, int64_t s_st,
+                unsigned long long* spike_count, void* stream);
+
+/* (b) selective scan -- SelectiveSSMLayer._discretize + _scan_sequential
+ * (ssm.py:106-139,184-221).  A = -exp(log_A); A_bar = exp(A*dt);
+ * B_bar = (A_bar-1)/A*B (dt*B where |A| < 1e-6); h = A_bar*h + B_bar*u;
+ * y = sum_n C[n]*h[n] + D*u.  If gate != NULL the output is y*silu(gate)
+ * (fused.py:130).  u, dt, gate, y: [B,T,d] contiguous in `dtype`;
+ * Bm, Cm: [B,T,N] contiguous in `dtype`; log_A: [d,N], D: [d] in `dtype`.
+ * state_in/state_out: [B,d,N] in `state_dtype` (state_in NULL = zeros); the
+ * recurrence itself runs in float32.  d_state N <= 256. */
+NT_API int nt_selective_scan(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d, int64_t N,
+                      const void* u, const void* dt, const void* Bm, const void* Cm,
+                      const void* log_A, const void* D, const void* gate,
+                      const void* state_in, void* state_out, void* y, void* stream);
+
+/* SelectiveSSMLayer.forward (ssm.py:313-349): B = u W_B^T, C = u W_C^T,
+ * dt = softplus(u W_dt^T + b_dt), then the scan above.  W_proj is the packed
+ * projection weight [d + 2N, d] = rows of W_dt, then W_B, then W_C.
+ * Workspace: nt_ssm_workspace_bytes(). */
+NT_API int64_t nt_ssm_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t d, int64_t N);
+NT_API int nt_ssm_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d, int64_t N,
+                   const void* u, const void* W_proj, const void* b_dt,
+                   const void* log_A, const void* D,
+                   const void* state_in, void* state_out, void* y,
+                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/* (c) spike-sparse out_proj -- FusedSpikeBlock._sparse_out_proj
+ * (fused.py:149-165).  o: [M,K], spikes: [M,K] (0/1), W: [Nout,K], out:
+ * [M,Nout], all `dtype`, contiguous.  A row is active when any spike in it
+ * is non-zero.  If 2*n_active > M every row is projected (dense branch);
+ * otherwise only active rows are projected and inactive rows are zero.
+ * n_active_out: optional device int64 receiving n_active.
+ * Workspace: nt_sparse_out_proj_workspace_bytes(). */
+NT_API int64_t nt_sparse_out_proj_workspace_bytes(int dtype, int64_t M, int64_t K, int64_t Nout);
+NT_API int nt_sparse_out_proj(int dtype, int64_t M, int64_t K, int64_t Nout,
+                       const void* o, const void* spikes, const void* W, void* out,
+                       long long* n_active_out,
+                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/* (d) RMSNorm + in_proj -- fused.py:118-119.  xn = RMSNorm(x) (eps = float32
+ * machine epsilon, as nn.RMSNorm with eps=None), [h | gate] = xn W_in^T.
+ * x: [M,dm]; gamma: [dm]; W_in: [2*di, dm]; h, gate: [M,di], all `dtype`.
+ * Workspace: nt_rmsnorm_in_proj_workspace_bytes(). */
+NT_API int64_t nt_rmsnorm_in_proj_workspace_bytes(int dtype, int64_t M, int64_t dm, int64_t di);
+NT_API int nt_rmsnorm_in_proj(int dtype, int64_t M, int64_t dm, int64_t di,
+                       const void* x, const void* gamma, const void* W_in,
+                       void* h, void* gate,
+                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/* FusedSpikeBlock.forward in eval mode (fused.py:101-147):
+ *   out = sparse_out_proj(SSM(LIF(in_proj(RMSNorm(x))_h)) * silu(gate)) * out_scale + x
+ * x, out: [B,T,dm]; weights as in the module (W_proj packed as above);
+ * beta = sigmoid(beta_logit) and threshold in `dtype`, [di];
+ * mem_in/mem_out: [B,di] in `dtype` (mem_in NULL = zeros);
+ * state_in/state_out: [B,di,N] in `state_dtype` (state_in NULL = zeros);
+ * spike_count: device uint64, incremented by this block's spike count;
+ * sparse: 1 = inference sparse out_proj (fused.py:133-134), 0 = dense.
+ * Workspace: nt_block_workspace_bytes(). */
+NT_API int64_t nt_block_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N);
+NT_API int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t dm, int64_t di,
+                     int64_t N,
+                     const void* x, const void* norm_w, const void* W_in,
+                     const void* beta, const void* threshold,
+                     const void* log_A, const void* D, const void* W_proj, const void* b_dt,
+                     const void* W_out, const void* out_scale,
+                     const void* mem_in, void* mem_out,
+                     const void* state_in, void* state_out,
+                     void* out, unsigned long long* spike_count, int sparse,
+                     void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Standalone fused LIF + selective scan: the LIF spikes of x drive the scan
+ * with caller-given dt/B/C.  x, delta, y: [B,L,d] bf16; Bm, Cm: [B,L,N] bf16;
+ * log_A: [d,N], Dskip, beta, threshold: [d] float32; mem_in/mem_out: [B,d]
+ * float32; state_in/state_out: [B,d,N] float32 (NULL inputs = zeros);
+ * spikes: optional [B,L,d] output in `spike_dtype` (NT_U8 or NT_BF16);
+ * spike_count: optional device uint64 (incremented).  All math in float32. */
+NT_API int nt_lif_ssm_fused(int64_t B, int64_t L, int64_t d, int64_t N,
+                     const void* x, const void* delta, const void* Bm, const void* Cm,
+                     const float* log_A, const float* Dskip,
+                     const float* beta, const float* threshold,
+                     const float* mem_in, float* mem_out,
+                     const float* state_in, float* state_out,
+                     void* y, void* spikes, int spike_dtype,
+                     unsigned long long* spike_count, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEURATENSOR_NATIVE_H */

@@ -1,0 +1,50 @@
+"""Backend detection (the reference's ``neuratensor/backends/detect.py:34-70``) plus the native-kernel status."""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+
+@dataclass
+class BackendInfo:
+    name: str
+    device: str
+    dtype: torch.dtype
+    gpu_name: Optional[str] = None
+    compute_capability: Optional[str] = None
+    memory_gb: Optional[float] = None
+    bf16: bool = False
+    compile_ready: bool = False
+    native_kernels: bool = False
+    notes: list = field(default_factory=list)
+
+    def print(self) -> None:
+        print("=" * 52)
+        print(f"  Backend: {self.name}")
+        print(f"  Device:  {self.device}  dtype={self.dtype}")
+        if self.gpu_name:
+            print(f"  GPU:     {self.gpu_name}")
+            print(f"  CC:      {self.compute_capability}")
+            print(f"  VRAM:    {self.memory_gb:.1f} GB")
+            print(f"  BF16:    {self.bf16}")
+        print(f"  Native:  {self.native_kernels}")
+        for n in self.notes:
+            print(f"  !  {n}")
+        print("=" * 52)
+
+
+def detect_backend() -> BackendInfo:
+    from .native import native_available
+    if torch.cuda.is_available():
+        p = torch.cuda.get_device_properties(0)
+        ok = p.major == 10 and p.minor == 0
+        notes = [] if ok else [f"sm_{p.major}{p.minor} is not sm_100: the B200 kernels cannot run here"]
+        return BackendInfo(name="b200" if ok else "cuda", device="cuda",
+                           dtype=torch.bfloat16 if p.major >= 8 else torch.float16, gpu_name=p.name,
+                           compute_capability=f"{p.major}.{p.minor}", memory_gb=p.total_memory / 1024 ** 3,
+                           bf16=p.major >= 8, compile_ready=hasattr(torch, "compile"),
+                           native_kernels=ok and native_available(), notes=notes)
+    return BackendInfo(name="cpu", device="cpu", dtype=torch.float32, compile_ready=hasattr(torch, "compile"),
+                       notes=["No GPU detected: the B200 kernels need an sm_100 device"])

@@ -1,0 +1,279 @@
+"""NeuraTensorModel on the B200 block kernels.
+
+Interface mirror of NeuraTensor's ``neuratensor/core/model.py``:
+``ModelConfig`` (model.py:32-85), ``RotaryEmbedding`` / ``apply_rotary`` /
+``SlidingWindowAttention`` (model.py:88-181) and ``NeuraTensorModel``
+(model.py:184-396) keep their names, fields, submodule layout and
+initialisation order (embedding, blocks with attention interleaved, final
+norm, tied lm_head, then ``_init_weights``), so a seed gives the reference's
+weights and checkpoints load either way.
+
+The spike blocks run on the native kernels.  The glue around them
+(embedding gather, sliding-window attention, final RMSNorm, lm_head) stays
+in torch, as in the reference.  The forward collects every block's spike
+count in one device buffer and reads it once, instead of the reference's
+three host syncs per block.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+from torch import Tensor
+
+from .fused import BlockState, FusedSpikeBlock, rate_like_reference
+
+
+@dataclass
+class ModelConfig:
+    """Full model configuration (model.py:32-85)."""
+    vocab_size: int = 32_000
+    d_model: int = 512
+    n_layers: int = 8
+    d_state: int = 16
+    expand: int = 2
+    beta_init: float = 0.9
+    learn_beta: bool = True
+    dropout: float = 0.0
+    tie_weights: bool = True
+    max_seq_len: int = 2048
+    attn_every: int = 0
+    attn_heads: int = 4
+    attn_window: int = 256
+    model_name: str = "custom"
+
+    @property
+    def n_attn_layers(self) -> int:
+        return 0 if self.attn_every <= 0 else self.n_layers // self.attn_every
+
+    def n_params_estimate(self) -> int:
+        di = self.d_model * self.expand
+        block = (2 * self.d_model + 4 * self.d_model * di + di + 2 * di * self.d_state + di * di + di
+                 + di * self.d_state + di + 1)
+        attn = (2 * self.d_model + 4 * self.d_model * self.d_model) if self.attn_every > 0 else 0
+        head = 0 if self.tie_weights else self.vocab_size * self.d_model
+        return self.vocab_size * self.d_model + self.n_layers * block + self.n_attn_layers * attn + head
+
+
+class RotaryEmbedding(nn.Module):
+    """Rotary position embedding tables (model.py:88-116)."""
+
+    def __init__(self, dim: int, max_seq_len: int = 8192, base: float = 10000.0) -> None:
+        super().__init__()
+        inv_freq = 1.0 / (base ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim))
+        self.register_buffer("inv_freq", inv_freq, persistent=False)
+        self._max_cached = 0
+        self.register_buffer("cos_cached", torch.empty(0), persistent=False)
+        self.register_buffer("sin_cached", torch.empty(0), persistent=False)
+
+    def _build_cache(self, seq_len: int, device, dtype) -> None:
+        if seq_len <= self._max_cached and self.cos_cached.dtype == dtype and self.cos_cached.device == device:
+            return
+        self._max_cached = seq_len
+        pos = torch.arange(seq_len, device=device, dtype=torch.float32)
+        ang = torch.outer(pos, self.inv_freq.to(device))
+        ang = torch.cat([ang, ang], dim=-1)
+        self.cos_cached = ang.cos().to(dtype)
+        self.sin_cached = ang.sin().to(dtype)
+
+    def forward(self, x: Tensor, offset: int = 0) -> Tuple[Tensor, Tensor]:
+        T = x.shape[-2]
+        self._build_cache(offset + T, x.device, x.dtype)
+        return self.cos_cached[offset:offset + T], self.sin_cached[offset:offset + T]
+
+
+def _rotate_half(x: Tensor) -> Tensor:
+    a, b = x.chunk(2, dim=-1)
+    return torch.cat([-b, a], dim=-1)
+
+
+def apply_rotary(x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
+    """RoPE on x [B, H, T, hd]."""
+    return x * cos + _rotate_half(x) * sin
+
+
+class SlidingWindowAttention(nn.Module):
+    """Causal multi-head attention limited to the last ``window`` keys (model.py:129-181).
+
+    For T <= window plain causal attention; for T > window query i sees keys
+    j with i - window <= j <= i.  Stateless across calls, like the reference
+    (a T=1 decode step attends to itself only).
+    """
+
+    def __init__(self, d_model: int, n_heads: int = 4, window: int = 256, max_seq_len: int = 8192) -> None:
+        super().__init__()
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.head_dim = d_model // n_heads
+        self.window = window
+        self.norm = nn.RMSNorm(d_model)
+        self.qkv = nn.Linear(d_model, d_model * 3, bias=False)
+        self.o_proj = nn.Linear(d_model, d_model, bias=False)
+        self.rope = RotaryEmbedding(self.head_dim, max_seq_len=max_seq_len)
+        self._mask = None
+
+    def _window_mask(self, T: int, device) -> Tensor:
+        if self._mask is None or self._mask.shape[-1] != T or self._mask.device != device:
+            i = torch.arange(T, device=device)
+            rel = i[:, None] - i[None, :]
+            self._mask = ((rel >= 0) & (rel <= self.window))[None, None]
+        return self._mask
+
+    def forward(self, x: Tensor) -> Tensor:
+        B, T, _ = x.shape
+        h = self.norm(x)
+        q, k, v = self.qkv(h).view(B, T, 3, self.n_heads, self.head_dim).permute(2, 0, 3, 1, 4).unbind(0)
+        cos, sin = self.rope(q)
+        q = apply_rotary(q, cos, sin)
+        k = apply_rotary(k, cos, sin)
+        if T <= self.window:
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        else:
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=self._window_mask(T, x.device))
+        return self.o_proj(o.transpose(1, 2).reshape(B, T, self.d_model)) + x
+
+
+class NeuraTensorModel(nn.Module):
+    """Embedding -> FusedSpikeBlocks (+ attention every ``attn_every``) -> RMSNorm -> tied lm_head."""
+
+    def __init__(self, config: ModelConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.embedding = nn.Embedding(config.vocab_size, config.d_model)
+        self.blocks = nn.ModuleList()
+        self.attn_layers = nn.ModuleDict()
+        for i in range(config.n_layers):
+            self.blocks.append(FusedSpikeBlock(d_model=config.d_model, d_state=config.d_state,
+                                               expand=config.expand, beta_init=config.beta_init,
+                                               learn_beta=config.learn_beta, dropout=config.dropout))
+            if config.attn_every > 0 and (i + 1) % config.attn_every == 0:
+                self.attn_layers[str(i)] = SlidingWindowAttention(d_model=config.d_model, n_heads=config.attn_heads,
+                                                                  window=config.attn_window,
+                                                                  max_seq_len=config.max_seq_len)
+        self.norm = nn.RMSNorm(config.d_model)
+        self.lm_head = nn.Linear(config.d_model, config.vocab_size, bias=False)
+        if config.tie_weights:
+            self.lm_head.weight = self.embedding.weight
+        self._init_weights()
+        self._ws = None
+
+    def _init_weights(self) -> None:
+        nn.init.normal_(self.embedding.weight, std=0.02)
+        for blk in self.blocks:
+            nn.init.xavier_uniform_(blk.in_proj.weight)
+            nn.init.xavier_uniform_(blk.out_proj.weight)
+        for attn in self.attn_layers.values():
+            nn.init.xavier_uniform_(attn.qkv.weight)
+            nn.init.xavier_uniform_(attn.o_proj.weight)
+
+    @classmethod
+    def from_preset(cls, name: str) -> "NeuraTensorModel":
+        from ..config.presets import get_preset
+        return cls(get_preset(name))
+
+    def _workspace(self, x: Tensor) -> Tensor:
+        """One block workspace reused by every block of a forward."""
+        from .. import native
+        c = self.config
+        B, T, _ = x.shape
+        n = native.block_workspace_bytes(x.dtype, B, T, c.d_model, c.d_model * c.expand, c.d_state)
+        ws = getattr(self, "_ws", None)
+        if ws is None or ws.numel() < n or ws.device != x.device:
+            self._ws = torch.empty(n, dtype=torch.uint8, device=x.device)
+        return self._ws
+
+    def forward_device(self, input_ids: Tensor, states: Optional[List[Optional[BlockState]]] = None):
+        """Forward without any host sync: returns (logits, states, per-layer spike counts on device)."""
+        if states is None:
+            states = [None] * len(self.blocks)
+        if input_ids.shape[1] > self.config.max_seq_len:
+            import warnings
+            warnings.warn(f"Input sequence length {input_ids.shape[1]} exceeds max_seq_len "
+                          f"{self.config.max_seq_len}; truncating.", UserWarning, stacklevel=3)
+            input_ids = input_ids[:, : self.config.max_seq_len]
+        x = self.embedding(input_ids)
+        counts = torch.zeros(len(self.blocks), dtype=torch.int64, device=x.device)
+        ws = self._workspace(x)
+        new_states: List[BlockState] = []
+        with torch.no_grad():
+            for i, (blk, st) in enumerate(zip(self.blocks, states)):
+                x, ns = blk.forward_native(x, st, counts[i], workspace=ws)
+                new_states.append(ns)
+                key = str(i)
+                if key in self.attn_layers:
+                    x = self.attn_layers[key](x)
+            logits = self.lm_head(self.norm(x))
+        return logits, new_states, counts
+
+    def metrics_from_counts(self, counts: List[int], numel: int, dtype: torch.dtype) -> Dict:
+        rates = [rate_like_reference(c, numel, dtype) for c in counts]
+        mean = sum(rates) / len(rates)
+        return {"spike_rate": mean, "per_layer_spike_rate": rates, "estimated_sparsity_pct": (1.0 - mean) * 100}
+
+    def forward(self, input_ids: Tensor, states: Optional[List[Optional[BlockState]]] = None
+                ) -> Tuple[Tensor, List[BlockState], Dict]:
+        """input_ids [B, T] -> (logits [B, T, vocab], states, metrics) (model.py:240-293)."""
+        logits, new_states, counts = self.forward_device(input_ids, states)
+        B, T = logits.shape[:2]
+        di = self.config.d_model * self.config.expand
+        metrics = self.metrics_from_counts(counts.tolist(), B * T * di, logits.dtype)
+        return logits, new_states, metrics
+
+    def count_parameters(self) -> int:
+        return sum(p.numel() for p in self.parameters())
+
+    def count_trainable_parameters(self) -> int:
+        return sum(p.numel() for p in self.parameters() if p.requires_grad)
+
+    @torch.no_grad()
+    def generate(self, input_ids: Tensor, max_new_tokens: int = 50, temperature: float = 1.0, top_k: int = 50,
+                 top_p: float = 1.0, repetition_penalty: float = 1.0, stop_tokens: Optional[List[int]] = None,
+                 states: Optional[List[Optional[BlockState]]] = None) -> Tuple[Tensor, List[BlockState]]:
+        """Autoregressive sampling with carried block state (model.py:301-370)."""
+        self.eval()
+        out = input_ids
+        stop = set(stop_tokens or [])
+        logits, states, _ = self.forward_device(out, states)
+        nxt_logits = logits[:, -1, :]
+        for _ in range(max_new_tokens):
+            if repetition_penalty != 1.0:
+                for b in range(out.shape[0]):
+                    for tok in out[b].tolist():
+                        v = nxt_logits[b, tok]
+                        nxt_logits[b, tok] = v / repetition_penalty if v > 0 else v * repetition_penalty
+            if temperature != 1.0:
+                nxt_logits = nxt_logits / temperature
+            if top_k > 0:
+                kth = torch.topk(nxt_logits, min(top_k, nxt_logits.size(-1))).values[:, [-1]]
+                nxt_logits[nxt_logits < kth] = float("-inf")
+            if top_p < 1.0:
+                srt, idx = torch.sort(nxt_logits, descending=True, dim=-1)
+                p = torch.softmax(srt, dim=-1)
+                drop = p.cumsum(-1) - p > top_p
+                srt = srt.masked_fill(drop, float("-inf"))
+                nxt_logits = torch.zeros_like(nxt_logits).scatter_(-1, idx, srt)
+            tok = torch.multinomial(torch.softmax(nxt_logits, dim=-1), num_samples=1)
+            out = torch.cat([out, tok], dim=1)
+            if stop and tok.item() in stop:
+                break
+            logits, states, _ = self.forward_device(tok, states)
+            nxt_logits = logits[:, -1, :]
+        return out, states
+
+    def info(self) -> str:
+        c = self.config
+        rows = [("Parameters", f"{self.count_parameters():,}"), ("Layers", c.n_layers), ("d_model", c.d_model),
+                ("d_state", c.d_state), ("expand", c.expand), ("vocab", f"{c.vocab_size:,}"),
+                ("max_seq_len", c.max_seq_len)]
+        if c.attn_every > 0:
+            rows += [("attn_every", c.attn_every), ("attn_heads", c.attn_heads), ("attn_window", c.attn_window),
+                     ("attn_layers", c.n_attn_layers)]
+        bar = "=" * 60
+        body = "\n".join(f"  {k + ':':<14} {v:>14}" for k, v in rows)
+        return f"{bar}\n  NeuraTensor v4 (B200 kernels) -- {c.model_name.upper()}\n{bar}\n{body}\n{bar}"
+
+
+NeuraTensor = NeuraTensorModel

@@ -1,0 +1,400 @@
+// C ABI of libneuratensor_native.so: argument checks, workspace carving and
+// kernel sequencing.  Declarations and the reference interfaces each entry
+// point replaces are in include/neuratensor_native.h.
+#include "nt_kernels.cuh"
+
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+
+namespace nt {
+
+// ---------------------------------------------------------------------------
+// Errors
+// ---------------------------------------------------------------------------
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(NT_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+    return NT_OK;
+}
+
+// One error word per device, in this library's own device memory.
+__device__ unsigned g_error_word;
+
+unsigned* device_error_word(int device) {
+    static unsigned* ptrs[64] = {};
+    static std::mutex mu;
+    if (device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[device]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_error_word) == cudaSuccess) ptrs[device] = static_cast<unsigned*>(p);
+    }
+    return ptrs[device];
+}
+
+}  // namespace nt
+
+using namespace nt;
+
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int64_t esize(int dtype) { return dtype == NT_F32 ? 4 : (dtype == NT_BF16 ? 2 : 1); }
+
+inline bool act_dtype_ok(int dtype) { return dtype == NT_F32 || dtype == NT_BF16; }
+
+inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+// Sequential carving of a caller-provided workspace.
+struct Carve {
+    char* base;
+    int64_t off = 0;
+    explicit Carve(void* b) : base(static_cast<char*>(b)) {}
+    template <typename T> T* take(int64_t bytes) {
+        T* p = reinterpret_cast<T*>(base ? base + off : nullptr);
+        off += align256(bytes);
+        return p;
+    }
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int check_gemm_operand(const void* p, int64_t ld, int dtype, const char* name) {
+    if (dtype == NT_BF16 && (!aligned16(p) || (ld * 2) % 16))
+        return fail(NT_ERR_ARG, "%s: bf16 GEMM operands need 16-byte alignment and a row length multiple of 8", name);
+    return NT_OK;
+}
+
+// Workspace layouts ---------------------------------------------------------
+struct SsmWs { void* dt; void* bc; int64_t bytes; };
+SsmWs ssm_ws(void* ws, int dtype, int64_t M, int64_t d, int64_t N) {
+    Carve c(ws);
+    SsmWs w;
+    w.dt = c.take<char>(M * d * esize(dtype));
+    w.bc = c.take<char>(M * 2 * N * esize(dtype));
+    w.bytes = c.off;
+    return w;
+}
+
+struct SparseWs { unsigned char* flags; int* pos; int* idx; int* counters; void* oc; int64_t bytes; };
+SparseWs sparse_ws(void* ws, int dtype, int64_t M, int64_t K) {
+    Carve c(ws);
+    SparseWs w;
+    w.flags = c.take<unsigned char>(M);
+    w.pos = c.take<int>(M * 4);
+    w.idx = c.take<int>(M * 4);
+    w.counters = c.take<int>(64);
+    w.oc = c.take<char>(M * K * esize(dtype));
+    w.bytes = c.off;
+    return w;
+}
+
+struct BlockWs {
+    void *xn, *h, *gate, *spikes, *dt, *bc, *o;
+    unsigned short* partials;
+    unsigned char* flags;
+    int *pos, *idx, *counters;
+    int64_t bytes;
+};
+BlockWs block_ws(void* ws, int dtype, int64_t M, int64_t dm, int64_t di, int64_t N) {
+    Carve c(ws);
+    BlockWs w;
+    const int64_t es = esize(dtype);
+    w.xn = c.take<char>(M * dm * es);
+    w.h = c.take<char>(M * di * es);
+    w.gate = c.take<char>(M * di * es);
+    w.spikes = c.take<char>(M * di * es);
+    w.dt = c.take<char>(M * di * es);
+    w.bc = c.take<char>(M * 2 * N * es);
+    w.o = c.take<char>(M * di * es);
+    w.partials = c.take<unsigned short>(M * ((di + 127) / 128) * 2);
+    w.flags = c.take<unsigned char>(M);
+    w.pos = c.take<int>(M * 4);
+    w.idx = c.take<int>(M * 4);
+    w.counters = c.take<int>(64);
+    w.bytes = c.off;
+    return w;
+}
+
+#define NT_TRY(expr)                  \
+    do {                              \
+        int _rc = (expr);             \
+        if (_rc != NT_OK) return _rc; \
+    } while (0)
+
+}  // namespace
+
+extern "C" {
+
+int nt_abi_version(void) { return NT_ABI_VERSION; }
+
+const char* nt_last_error(void) { return g_last_error; }
+
+int nt_device_supported(int device) {
+    cudaDeviceProp p;
+    cudaError_t e = cudaGetDeviceProperties(&p, device);
+    if (e != cudaSuccess) return fail(NT_ERR_CUDA, "cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+    if (p.major != 10 || p.minor != 0)
+        return fail(NT_ERR_ARCH, "device %d is sm_%d%d; this library is built for sm_100a", device, p.major, p.minor);
+    return NT_OK;
+}
+
+int nt_get_error_flag(int device, unsigned* flags, int clear) {
+    if (!flags) return fail(NT_ERR_ARG, "nt_get_error_flag: flags is NULL");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return fail(NT_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    int rc = NT_OK;
+    unsigned* w = device_error_word(device);
+    if (!w) rc = fail(NT_ERR_CUDA, "error word unavailable");
+    else if (cudaDeviceSynchronize() != cudaSuccess ||
+             cudaMemcpy(flags, w, sizeof(unsigned), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = fail(NT_ERR_CUDA, "reading the device error word failed: %s", cudaGetErrorString(cudaGetLastError()));
+    else if (clear && cudaMemset(w, 0, sizeof(unsigned)) != cudaSuccess)
+        rc = fail(NT_ERR_CUDA, "clearing the device error word failed");
+    cudaSetDevice(prev);
+    return rc;
+}
+
+// ---------------------------------------------------------------------------
+// (a) LIF
+// ---------------------------------------------------------------------------
+int nt_lif_scan(int dtype, int64_t B, int64_t T, int64_t C, const void* x, int64_t x_sb, int64_t x_st,
+                const void* beta, const void* threshold, const void* mem_in, void* mem_out, void* spikes,
+                int64_t s_sb, int64_t s_st, unsigned long long* spike_count, void* stream) {
+    if (!act_dtype_ok(dtype)) return fail(NT_ERR_DTYPE, "nt_lif_scan: dtype %d", dtype);
+    if (B < 1 || T < 1 || C < 1) return fail(NT_ERR_ARG, "nt_lif_scan: B, T, C must be >= 1 (got %lld, %lld, %lld)",
+                                             (long long)B, (long long)T, (long long)C);
+    if (!x || !beta || !threshold || !mem_out || !spikes) return fail(NT_ERR_ARG, "nt_lif_scan: null pointer");
+    if (B > 65535) return fail(NT_ERR_ARG, "nt_lif_scan: B > 65535");
+    LifArgs a{B, T, C, x, x_sb, x_st, beta, threshold, mem_in, mem_out, spikes, s_sb, s_st, spike_count, nullptr, 0};
+    return launch_lif_scan(dtype, dtype, a, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// (b) selective scan
+// ---------------------------------------------------------------------------
+int nt_selective_scan(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d, int64_t N, const void* u,
+                      const void* dt, const void* Bm, const void* Cm, const void* log_A, const void* D,
+                      const void* gate, const void* state_in, void* state_out, void* y, void* stream) {
+    if (!act_dtype_ok(dtype) || !act_dtype_ok(state_dtype)) return fail(NT_ERR_DTYPE, "nt_selective_scan: dtype");
+    if (B < 1 || T < 1 || d < 1 || N < 1) return fail(NT_ERR_ARG, "nt_selective_scan: sizes must be >= 1");
+    if (N > 256) return fail(NT_ERR_ARG, "nt_selective_scan: d_state %lld > 256", (long long)N);
+    if (B > 65535) return fail(NT_ERR_ARG, "nt_selective_scan: B > 65535");
+    if (!u || !dt || !Bm || !Cm || !log_A || !D || !state_out || !y)
+        return fail(NT_ERR_ARG, "nt_selective_scan: null pointer");
+    ScanArgs a{B, T, d, N, u, dt, Bm, Cm, N, log_A, D, gate, state_in, state_out, y, nullptr, nullptr};
+    return launch_selective_scan(dtype, state_dtype, a, as_stream(stream));
+}
+
+int64_t nt_ssm_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t d, int64_t N) {
+    return ssm_ws(nullptr, dtype, B * T, d, N).bytes;
+}
+
+int nt_ssm_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d, int64_t N, const void* u,
+                   const void* W_proj, const void* b_dt, const void* log_A, const void* D, const void* state_in,
+                   void* state_out, void* y, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!act_dtype_ok(dtype) || !act_dtype_ok(state_dtype)) return fail(NT_ERR_DTYPE, "nt_ssm_forward: dtype");
+    if (B < 1 || T < 1 || d < 1 || N < 1 || N > 256) return fail(NT_ERR_ARG, "nt_ssm_forward: bad sizes");
+    if (!u || !W_proj || !b_dt || !log_A || !D || !state_out || !y) return fail(NT_ERR_ARG, "nt_ssm_forward: null pointer");
+    const int64_t M = B * T;
+    SsmWs w = ssm_ws(workspace, dtype, M, d, N);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(NT_ERR_WORKSPACE, "nt_ssm_forward: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                    (long long)w.bytes);
+    NT_TRY(check_gemm_operand(u, d, dtype, "nt_ssm_forward(u)"));
+    NT_TRY(check_gemm_operand(W_proj, d, dtype, "nt_ssm_forward(W_proj)"));
+    cudaStream_t st = as_stream(stream);
+    GemmArgs g{};
+    g.M = M; g.N = d + 2 * N; g.K = d;
+    g.A = u; g.lda = d; g.Bw = W_proj; g.ldb = d;
+    g.epi.kind = EPI_SSM_PROJ;
+    g.epi.out = w.dt; g.epi.ldo = d; g.epi.out2 = w.bc; g.epi.ldo2 = 2 * N; g.epi.split = d; g.epi.bias = b_dt;
+    NT_TRY(launch_gemm(dtype, g, st));
+    const char* bc = static_cast<const char*>(w.bc);
+    ScanArgs a{B, T, d, N, u, w.dt, bc, bc + N * esize(dtype), 2 * N, log_A, D, nullptr, state_in, state_out, y,
+               nullptr, nullptr};
+    return launch_selective_scan(dtype, state_dtype, a, st);
+}
+
+// ---------------------------------------------------------------------------
+// (c) sparse out_proj
+// ---------------------------------------------------------------------------
+int64_t nt_sparse_out_proj_workspace_bytes(int dtype, int64_t M, int64_t K, int64_t Nout) {
+    (void)Nout;
+    return sparse_ws(nullptr, dtype, M, K).bytes;
+}
+
+int nt_sparse_out_proj(int dtype, int64_t M, int64_t K, int64_t Nout, const void* o, const void* spikes,
+                       const void* W, void* out, long long* n_active_out, void* workspace, int64_t workspace_bytes,
+                       void* stream) {
+    if (!act_dtype_ok(dtype)) return fail(NT_ERR_DTYPE, "nt_sparse_out_proj: dtype %d", dtype);
+    if (M < 1 || K < 1 || Nout < 1) return fail(NT_ERR_ARG, "nt_sparse_out_proj: sizes must be >= 1");
+    if (!o || !spikes || !W || !out) return fail(NT_ERR_ARG, "nt_sparse_out_proj: null pointer");
+    SparseWs w = sparse_ws(workspace, dtype, M, K);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(NT_ERR_WORKSPACE, "nt_sparse_out_proj: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                    (long long)w.bytes);
+    NT_TRY(check_gemm_operand(o, K, dtype, "nt_sparse_out_proj(o)"));
+    NT_TRY(check_gemm_operand(W, K, dtype, "nt_sparse_out_proj(W)"));
+    if ((K * esize(dtype)) % 16) return fail(NT_ERR_ARG, "nt_sparse_out_proj: row bytes must be a multiple of 16");
+    cudaStream_t st = as_stream(stream);
+    NT_TRY(launch_row_any(dtype, M, K, spikes, w.flags, st));
+    NT_TRY(launch_compact_rows(M, w.flags, w.pos, w.idx, w.counters, n_active_out, 1, st));
+    NT_TRY(launch_gather_rows(dtype, M, K, o, w.idx, w.counters, w.oc, st));
+    GemmArgs g{};
+    g.M = M; g.N = Nout; g.K = K;
+    g.A = w.oc; g.lda = K; g.Bw = W; g.ldb = K; g.m_count = w.counters + 2;
+    g.epi.kind = EPI_SCATTER; g.epi.out = out; g.epi.ldo = Nout; g.epi.row_idx = w.idx;
+    NT_TRY(launch_gemm(dtype, g, st));
+    return launch_fill_inactive(dtype, M, Nout, w.pos, w.counters, nullptr, out, st);
+}
+
+// ---------------------------------------------------------------------------
+// (d) RMSNorm + in_proj
+// ---------------------------------------------------------------------------
+int64_t nt_rmsnorm_in_proj_workspace_bytes(int dtype, int64_t M, int64_t dm, int64_t di) {
+    (void)di;
+    return align256(M * dm * esize(dtype));
+}
+
+int nt_rmsnorm_in_proj(int dtype, int64_t M, int64_t dm, int64_t di, const void* x, const void* gamma,
+                       const void* W_in, void* h, void* gate, void* workspace, int64_t workspace_bytes,
+                       void* stream) {
+    if (!act_dtype_ok(dtype)) return fail(NT_ERR_DTYPE, "nt_rmsnorm_in_proj: dtype %d", dtype);
+    if (M < 1 || dm < 1 || di < 1) return fail(NT_ERR_ARG, "nt_rmsnorm_in_proj: sizes must be >= 1");
+    if (!x || !gamma || !W_in || !h || !gate) return fail(NT_ERR_ARG, "nt_rmsnorm_in_proj: null pointer");
+    const int64_t need = nt_rmsnorm_in_proj_workspace_bytes(dtype, M, dm, di);
+    if (!workspace || workspace_bytes < need)
+        return fail(NT_ERR_WORKSPACE, "nt_rmsnorm_in_proj: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                    (long long)need);
+    NT_TRY(check_gemm_operand(workspace, dm, dtype, "nt_rmsnorm_in_proj(x)"));
+    NT_TRY(check_gemm_operand(W_in, dm, dtype, "nt_rmsnorm_in_proj(W_in)"));
+    cudaStream_t st = as_stream(stream);
+    NT_TRY(launch_rmsnorm(dtype, M, dm, x, gamma, workspace, st));
+    GemmArgs g{};
+    g.M = M; g.N = 2 * di; g.K = dm;
+    g.A = workspace; g.lda = dm; g.Bw = W_in; g.ldb = dm;
+    g.epi.kind = EPI_SPLIT2; g.epi.out = h; g.epi.ldo = di; g.epi.out2 = gate; g.epi.ldo2 = di; g.epi.split = di;
+    return launch_gemm(dtype, g, st);
+}
+
+// ---------------------------------------------------------------------------
+// FusedSpikeBlock.forward
+// ---------------------------------------------------------------------------
+int64_t nt_block_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N) {
+    return block_ws(nullptr, dtype, B * T, dm, di, N).bytes;
+}
+
+int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N,
+                     const void* x, const void* norm_w, const void* W_in, const void* beta, const void* threshold,
+                     const void* log_A, const void* D, const void* W_proj, const void* b_dt, const void* W_out,
+                     const void* out_scale, const void* mem_in, void* mem_out, const void* state_in,
+                     void* state_out, void* out, unsigned long long* spike_count, int sparse, void* workspace,
+                     int64_t workspace_bytes, void* stream) {
+    if (!act_dtype_ok(dtype) || !act_dtype_ok(state_dtype)) return fail(NT_ERR_DTYPE, "nt_block_forward: dtype");
+    if (B < 1 || T < 1 || dm < 1 || di < 1 || N < 1) return fail(NT_ERR_ARG, "nt_block_forward: sizes must be >= 1");
+    if (N > 256) return fail(NT_ERR_ARG, "nt_block_forward: d_state %lld > 256", (long long)N);
+    if (B > 65535) return fail(NT_ERR_ARG, "nt_block_forward: B > 65535");
+    if (!x || !norm_w || !W_in || !beta || !threshold || !log_A || !D || !W_proj || !b_dt || !W_out || !out_scale ||
+        !mem_out || !state_out || !out)
+        return fail(NT_ERR_ARG, "nt_block_forward: null pointer");
+    const int64_t M = B * T;
+    BlockWs w = block_ws(workspace, dtype, M, dm, di, N);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(NT_ERR_WORKSPACE, "nt_block_forward: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                    (long long)w.bytes);
+    NT_TRY(check_gemm_operand(W_in, dm, dtype, "nt_block_forward(W_in)"));
+    NT_TRY(check_gemm_operand(W_proj, di, dtype, "nt_block_forward(W_proj)"));
+    NT_TRY(check_gemm_operand(W_out, di, dtype, "nt_block_forward(W_out)"));
+    if (dtype == NT_BF16 && (dm % 8 || di % 8)) return fail(NT_ERR_ARG, "nt_block_forward: bf16 needs d_model, d_inner multiples of 8");
+    cudaStream_t st = as_stream(stream);
+    const int64_t es = esize(dtype);
+
+    // (d) RMSNorm + in_proj -> h | gate
+    NT_TRY(launch_rmsnorm(dtype, M, dm, x, norm_w, w.xn, st));
+    {
+        GemmArgs g{};
+        g.M = M; g.N = 2 * di; g.K = dm;
+        g.A = w.xn; g.lda = dm; g.Bw = W_in; g.ldb = dm;
+        g.epi.kind = EPI_SPLIT2; g.epi.out = w.h; g.epi.ldo = di; g.epi.out2 = w.gate; g.epi.ldo2 = di; g.epi.split = di;
+        NT_TRY(launch_gemm(dtype, g, st));
+    }
+    // (a) LIF -> spikes, membrane, per-row counts
+    const int64_t n_cblk = (di + 127) / 128;
+    {
+        LifArgs a{B, T, di, w.h, T * di, di, beta, threshold, mem_in, mem_out, w.spikes, T * di, di,
+                  spike_count, w.partials, n_cblk};
+        NT_TRY(launch_lif_scan(dtype, dtype, a, st));
+    }
+    // row activity + compaction (the density decision of _sparse_out_proj)
+    NT_TRY(launch_row_any_partials(M, n_cblk, w.partials, w.flags, st));
+    NT_TRY(launch_compact_rows(M, w.flags, w.pos, w.idx, w.counters, nullptr, sparse ? 1 : 0, st));
+    // (b) dt | B | C projections of the spikes
+    {
+        GemmArgs g{};
+        g.M = M; g.N = di + 2 * N; g.K = di;
+        g.A = w.spikes; g.lda = di; g.Bw = W_proj; g.ldb = di;
+        g.epi.kind = EPI_SSM_PROJ; g.epi.out = w.dt; g.epi.ldo = di; g.epi.out2 = w.bc; g.epi.ldo2 = 2 * N;
+        g.epi.split = di; g.epi.bias = b_dt;
+        NT_TRY(launch_gemm(dtype, g, st));
+    }
+    // (b) selective scan with the gate fused, rows compacted when sparse
+    {
+        const char* bc = static_cast<const char*>(w.bc);
+        ScanArgs a{B, T, di, N, w.spikes, w.dt, bc, bc + N * es, 2 * N, log_A, D, w.gate, state_in, state_out, w.o,
+                   w.pos, w.counters + 1};
+        NT_TRY(launch_selective_scan(dtype, state_dtype, a, st));
+    }
+    // (c) out_proj on the processed rows, * out_scale + residual, scattered back
+    {
+        GemmArgs g{};
+        g.M = M; g.N = dm; g.K = di;
+        g.A = w.o; g.lda = di; g.Bw = W_out; g.ldb = di; g.m_count = w.counters + 2;
+        g.epi.kind = EPI_OUT_PROJ; g.epi.out = out; g.epi.ldo = dm; g.epi.scale = out_scale; g.epi.resid = x;
+        g.epi.ldr = dm; g.epi.row_idx = w.idx;
+        NT_TRY(launch_gemm(dtype, g, st));
+    }
+    // rows skipped by the sparse branch: out = 0 * out_scale + x = x
+    return launch_fill_inactive(dtype, M, dm, w.pos, w.counters, x, out, st);
+}
+
+// ---------------------------------------------------------------------------
+// Standalone fused LIF + selective scan
+// ---------------------------------------------------------------------------
+int nt_lif_ssm_fused(int64_t B, int64_t L, int64_t d, int64_t N, const void* x, const void* delta, const void* Bm,
+                     const void* Cm, const float* log_A, const float* Dskip, const float* beta,
+                     const float* threshold, const float* mem_in, float* mem_out, const float* state_in,
+                     float* state_out, void* y, void* spikes, int spike_dtype, unsigned long long* spike_count,
+                     void* stream) {
+    if (B < 1 || L < 1 || d < 1 || N < 1 || N > 256) return fail(NT_ERR_ARG, "nt_lif_ssm_fused: bad sizes");
+    if (B > 65535) return fail(NT_ERR_ARG, "nt_lif_ssm_fused: B > 65535");
+    if (!x || !delta || !Bm || !Cm || !log_A || !Dskip || !beta || !threshold || !mem_out || !state_out || !y)
+        return fail(NT_ERR_ARG, "nt_lif_ssm_fused: null pointer");
+    if (spikes && spike_dtype != NT_U8 && spike_dtype != NT_BF16)
+        return fail(NT_ERR_DTYPE, "nt_lif_ssm_fused: spike dtype %d", spike_dtype);
+    FusedArgs f{B, L, d, N, x, delta, Bm, Cm, log_A, Dskip, beta, threshold, mem_in, mem_out, state_in, state_out,
+                y, spikes, spike_dtype, spike_count};
+    return launch_lif_ssm_fused(f, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,372 @@
+// GEMMs of the block: D[M,N] = A[M,K] * W[N,K]^T with fused epilogues.
+//
+//  * bf16: a tcgen05 tensor-core kernel.  TMA (cp.async.bulk.tensor, 128-byte
+//    swizzle) streams A and W tiles into a STAGES-deep shared-memory ring;
+//    one elected thread issues tcgen05.mma (kind::f16, fp32 accumulation in
+//    TMEM); four epilogue warps read the 128 x BN accumulator back with
+//    tcgen05.ld and apply the epilogue (softplus for dt, out_scale +
+//    residual + row scatter for out_proj, ...).
+//  * fp32: the reference's fp32 mode needs fp32 products; a tiled CUDA-core
+//    kernel with the same epilogues.
+//
+// Every mbarrier wait is bounded: on expiry the kernel raises a bit in the
+// device error word and winds down instead of spinning forever.
+#include "nt_kernels.cuh"
+
+#include <cuda.h>
+#include <mutex>
+
+namespace nt {
+
+// ---------------------------------------------------------------------------
+// Epilogue (per element; rounding points follow the reference's tensor ops)
+// ---------------------------------------------------------------------------
+template <int DT, int KIND>
+__device__ __forceinline__ void epi_apply(const EpiArgs& e, int64_t row, int64_t col, float acc) {
+    using E = Elem<DT>;
+    using T = typename E::T;
+    if (KIND == EPI_STORE) {
+        static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(acc);
+    } else if (KIND == EPI_SPLIT2) {
+        if (col < e.split) static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(acc);
+        else static_cast<T*>(e.out2)[row * e.ldo2 + (col - e.split)] = E::from_f(acc);
+    } else if (KIND == EPI_SSM_PROJ) {
+        if (col < e.split) {
+            // dt = softplus(u W_dt^T + b_dt)  (ssm.py:330; threshold 20)
+            const float v = E::rnd(acc + E::load(static_cast<const T*>(e.bias) + col));
+            const float sp = v > 20.f ? v : log1pf(expf(v));
+            static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(sp);
+        } else {
+            static_cast<T*>(e.out2)[row * e.ldo2 + (col - e.split)] = E::from_f(acc);
+        }
+    } else if (KIND == EPI_OUT_PROJ) {
+        // out = out_proj(o) * out_scale + residual  (fused.py:138)
+        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+        const float s = E::load(static_cast<const T*>(e.scale));
+        float v = E::rnd(acc);
+        v = E::rnd(v * s);
+        v = E::rnd(v + E::load(static_cast<const T*>(e.resid) + r * e.ldr + col));
+        static_cast<T*>(e.out)[r * e.ldo + col] = E::from_f(v);
+    } else {  // EPI_SCATTER
+        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+        static_cast<T*>(e.out)[r * e.ldo + col] = E::from_f(acc);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// PTX wrappers (sm_100a)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: false when the limit expired.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (kSpinLimit >> 2); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 64 bf16 (128 B), 8-row core-matrix groups 1024 B apart (SBO), version 1.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);        // start address
+    d |= (uint64_t)1 << 16;                         // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;               // SBO
+    d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                         // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, both K-major, M x N tile.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4)                 // D format f32
+         | (1u << 7)                 // A bf16
+         | (1u << 10)                // B bf16
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
+}
+
+constexpr int kBM = 128, kBK = 64;
+
+template <int BN, int STAGES>
+struct TcSmem {
+    __nv_bfloat16 a[STAGES][kBM * kBK];
+    __nv_bfloat16 b[STAGES][BN * kBK];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t acc;
+    uint32_t tmem_base;
+};
+
+template <int KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               int64_t M, int64_t N, int64_t K, const int* m_count, EpiArgs epi, unsigned* err) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte alignment for the swizzled tiles
+    const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
+    auto& S = *reinterpret_cast<TcSmem<BN, STAGES>*>(base);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m0 = (int64_t)blockIdx.y * kBM, n0 = (int64_t)blockIdx.x * BN;
+    const int64_t m_eff = m_count ? (int64_t)*m_count : M;
+    if (m0 >= m_eff) return;
+    const int nk = (int)((K + kBK - 1) / kBK);
+
+    if (threadIdx.x == 0) {
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&S.full[s]), 1);
+            mbar_init(smem_u32(&S.empty[s]), 1);
+        }
+        mbar_init(smem_u32(&S.acc), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&S.tmem_base)), "r"(BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem_base;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        constexpr uint32_t bytes = (uint32_t)((kBM + BN) * kBK * sizeof(__nv_bfloat16));
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            if (kb >= STAGES && !mbar_wait(smem_u32(&S.empty[s]), ((kb / STAGES) - 1) & 1)) {
+                atomicOr(err, ERRF_TIMEOUT_PRODUCER);
+                break;
+            }
+            mbar_expect_tx(smem_u32(&S.full[s]), bytes);
+            tma_load_2d(smem_u32(S.a[s]), &map_a, smem_u32(&S.full[s]), kb * kBK, (int)m0);
+            tma_load_2d(smem_u32(S.b[s]), &map_b, smem_u32(&S.full[s]), kb * kBK, (int)n0);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            if (!mbar_wait(smem_u32(&S.full[s]), (kb / STAGES) & 1)) {
+                atomicOr(err, ERRF_TIMEOUT_MMA);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(S.a[s]), sb = smem_u32(S.b[s]);
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+                // advance 16 bf16 (32 bytes) along K inside the swizzle atom
+                tc_mma(tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), idesc,
+                       (kb | k) ? 1u : 0u);
+            }
+            tc_commit(smem_u32(&S.empty[s]));
+        }
+        tc_commit(smem_u32(&S.acc));
+    } else if (warp >= 2) {
+        // ---------------- epilogue: TMEM -> registers -> global ----------------
+        const int q = warp & 3;                     // TMEM lane quarter this warp may access
+        const int64_t row = m0 + q * 32 + lane;
+        if (!mbar_wait(smem_u32(&S.acc), 0)) {
+            atomicOr(err, ERRF_TIMEOUT_EPILOGUE);
+        } else {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+                if (row < m_eff) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int64_t col = n0 + c + j;
+                        if (col < N) epi_apply<NT_BF16, KIND>(epi, row, col, v[j]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// fp32 CUDA-core GEMM (64 x 64 tile, 256 threads, 4 x 4 outputs per thread)
+// ---------------------------------------------------------------------------
+template <int KIND>
+__global__ void __launch_bounds__(256)
+gemm_f32_kernel(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* W, int64_t ldb,
+                const int* m_count, EpiArgs epi) {
+    __shared__ float As[16][64 + 4];
+    __shared__ float Ws[16][64 + 4];
+    const int64_t m_eff = m_count ? (int64_t)*m_count : M;
+    const int64_t m0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
+    if (m0 >= m_eff) return;
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    float acc[4][4] = {};
+    for (int64_t k0 = 0; k0 < K; k0 += 16) {
+        for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+            const int kk = i % 16, rr = i / 16;
+            const int64_t ra = m0 + rr, rb = n0 + rr, k = k0 + kk;
+            As[kk][rr] = (ra < m_eff && k < K) ? A[ra * lda + k] : 0.f;
+            Ws[kk][rr] = (rb < N && k < K) ? W[rb * ldb + k] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { a[i] = As[kk][ty * 4 + i]; b[i] = Ws[kk][tx * 4 + i]; }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t row = m0 + ty * 4 + i;
+        if (row >= m_eff) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t col = n0 + tx * 4 + j;
+            if (col < N) epi_apply<NT_F32, KIND>(epi, row, col, acc[i][j]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps through the driver entry point (no libcuda link)
+// ---------------------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode() {
+    static PFN_encodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] with leading dimension ld, box = box_rows x 64.
+static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    PFN_encodeTiled enc = get_encode();
+    if (!enc) return fail(NT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16)
+        return fail(NT_ERR_ARG, "gemm: operand must be 16-byte aligned with a leading dimension multiple of 8");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(NT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return NT_OK;
+}
+
+template <int KIND, int BN, int STAGES>
+static int launch_tc(const GemmArgs& g, cudaStream_t stream) {
+    CUtensorMap ma, mb;
+    int rc = make_map(&ma, g.A, g.M, g.K, g.lda, kBM);
+    if (rc) return rc;
+    rc = make_map(&mb, g.Bw, g.N, g.K, g.ldb, BN);
+    if (rc) return rc;
+    const size_t smem = sizeof(TcSmem<BN, STAGES>) + 1024;
+    auto kern = gemm_tc_kernel<KIND, BN, STAGES>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(NT_ERR_CUDA, "gemm: smem attribute: %s", cudaGetErrorString(e));
+    int dev = 0;
+    cudaGetDevice(&dev);
+    dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + kBM - 1) / kBM));
+    kern<<<grid, 192, smem, stream>>>(ma, mb, g.M, g.N, g.K, g.m_count, g.epi, device_error_word(dev));
+    return check_launch("gemm_tc_kernel");
+}
+
+template <int KIND>
+static int launch_kind(int dtype, const GemmArgs& g, cudaStream_t stream) {
+    if (dtype == NT_BF16) return launch_tc<KIND, 128, 4>(g, stream);
+    dim3 grid((unsigned)((g.N + 63) / 64), (unsigned)((g.M + 63) / 64));
+    gemm_f32_kernel<KIND><<<grid, 256, 0, stream>>>(g.M, g.N, g.K, static_cast<const float*>(g.A), g.lda,
+                                                     static_cast<const float*>(g.Bw), g.ldb, g.m_count, g.epi);
+    return check_launch("gemm_f32_kernel");
+}
+
+int launch_gemm(int dtype, const GemmArgs& g, cudaStream_t stream) {
+    if (dtype != NT_F32 && dtype != NT_BF16) return fail(NT_ERR_DTYPE, "gemm: dtype %d", dtype);
+    if (g.M <= 0 || g.N <= 0 || g.K <= 0) return NT_OK;
+    switch (g.epi.kind) {
+        case EPI_STORE: return launch_kind<EPI_STORE>(dtype, g, stream);
+        case EPI_SPLIT2: return launch_kind<EPI_SPLIT2>(dtype, g, stream);
+        case EPI_SSM_PROJ: return launch_kind<EPI_SSM_PROJ>(dtype, g, stream);
+        case EPI_OUT_PROJ: return launch_kind<EPI_OUT_PROJ>(dtype, g, stream);
+        case EPI_SCATTER: return launch_kind<EPI_SCATTER>(dtype, g, stream);
+        default: return fail(NT_ERR_ARG, "gemm: epilogue kind %d", g.epi.kind);
+    }
+}
+
+}  // namespace nt

@@ -1,0 +1,97 @@
+// Internal kernel argument blocks and launchers (not part of the C ABI).
+#pragma once
+#include "nt_common.cuh"
+
+namespace nt {
+
+struct LifArgs {
+    int64_t B, T, C;
+    const void* x; int64_t x_sb, x_st;
+    const void* beta; const void* threshold;
+    const void* mem_in; void* mem_out;
+    void* spikes; int64_t s_sb, s_st;
+    unsigned long long* spike_count;       // optional, += spikes
+    unsigned short* row_partials;          // optional [B*T][n_cblk] per-row counts
+    int64_t n_cblk;                        // = ceil(C/128)
+};
+// math: NT_F32 (exact fp32 recurrence) or NT_BF16 (bf16 rounding after each op)
+int launch_lif_scan(int dtype, int math, const LifArgs& a, cudaStream_t stream);
+
+struct ScanArgs {
+    int64_t B, T, d, N;
+    const void* u; const void* dt; const void* Bm; const void* Cm;
+    int64_t ld_bc;                          // row stride of Bm / Cm (elements)
+    const void* log_A; const void* D; const void* gate;
+    const void* state_in; void* state_out;
+    void* y;
+    // Row compaction (block path): when row_pos != nullptr and *n_active_dense
+    // says the sparse branch is taken, output row r goes to row row_pos[r]
+    // (inactive rows are skipped).
+    const int* row_pos; const int* sparse_flag;
+};
+int launch_selective_scan(int dtype, int state_dtype, const ScanArgs& a, cudaStream_t stream);
+
+struct FusedArgs {
+    int64_t B, L, d, N;
+    const void* x; const void* delta; const void* Bm; const void* Cm;
+    const float* log_A; const float* Dskip; const float* beta; const float* threshold;
+    const float* mem_in; float* mem_out; const float* state_in; float* state_out;
+    void* y; void* spikes; int spike_dtype;
+    unsigned long long* spike_count;
+};
+int launch_lif_ssm_fused(const FusedArgs& a, cudaStream_t stream);
+
+// RMSNorm rows (eps = FLT_EPSILON), rounding like torch's rms_norm.
+int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w, void* y,
+                   cudaStream_t stream);
+
+// Row activity: flags[r] = any(spikes[r, :] != 0) for a dense [M,K] matrix.
+int launch_row_any(int dtype, int64_t M, int64_t K, const void* spikes, unsigned char* flags,
+                   cudaStream_t stream);
+// Row activity from LIF per-row partial counts [M][n_cblk].
+int launch_row_any_partials(int64_t M, int64_t n_cblk, const unsigned short* partials,
+                            unsigned char* flags, cudaStream_t stream);
+// Exclusive scan of flags -> row_pos (position among active rows, or -1),
+// row_idx (inverse map, first n_active entries), counters[0] = n_active,
+// counters[1] = 1 when the sparse branch is taken (2*n_active <= M).
+// n_active_out (optional) receives n_active as int64.
+int launch_compact_rows(int64_t M, const unsigned char* flags, int* row_pos, int* row_idx,
+                        int* counters, long long* n_active_out, int sparse_enabled,
+                        cudaStream_t stream);
+// Gather active rows of src [M,K] into dst [n_active,K] (dst row i = src row row_idx[i]).
+int launch_gather_rows(int dtype, int64_t M, int64_t K, const void* src, const int* row_idx,
+                       const int* counters, void* dst, cudaStream_t stream);
+// Rows skipped by the sparse branch: dst[r,:] = fill (0) or src[r,:] (residual copy).
+int launch_fill_inactive(int dtype, int64_t M, int64_t N, const int* row_pos, const int* counters,
+                         const void* src, void* dst, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// GEMM: D[M,N] = A[M,K] * B[N,K]^T with a fused epilogue.
+// ---------------------------------------------------------------------------
+enum EpiKind : int {
+    EPI_STORE = 0,        // D -> out (dtype), ldo
+    EPI_SPLIT2 = 1,       // cols [0,split) -> out, [split,N) -> out2 (in_proj h | gate)
+    EPI_SSM_PROJ = 2,     // cols [0,split): softplus(acc + bias) -> out (dt); rest -> out2 (B|C)
+    EPI_OUT_PROJ = 3,     // out[row_map(r)] = rnd(rnd(rnd(acc)*scale) + resid[row_map(r)])
+    EPI_SCATTER = 4       // out[row_map(r)] = acc  (sparse out_proj without scale)
+};
+struct EpiArgs {
+    int kind;
+    void* out; int64_t ldo;
+    void* out2; int64_t ldo2;
+    int64_t split;
+    const void* bias;          // EPI_SSM_PROJ
+    const void* scale;         // EPI_OUT_PROJ: pointer to one dtype value
+    const void* resid; int64_t ldr;
+    const int* row_idx;        // row map for compacted A rows (nullptr: identity)
+};
+struct GemmArgs {
+    int64_t M, N, K;
+    const void* A; int64_t lda;   // [M,K] row-major
+    const void* Bw; int64_t ldb;  // [N,K] row-major
+    const int* m_count;           // optional device row count (rows >= *m_count are skipped)
+    EpiArgs epi;
+};
+int launch_gemm(int dtype, const GemmArgs& g, cudaStream_t stream);
+
+}  // namespace nt

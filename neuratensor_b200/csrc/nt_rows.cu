@@ -1,0 +1,224 @@
+// Row-wise kernels: RMSNorm (neuratensor/core/fused.py:118, nn.RMSNorm with
+// eps=None) and the spike-row compaction behind the sparse out_proj
+// (neuratensor/core/fused.py:149-165).
+//
+// Compaction is a stream compaction over the per-row "any spike" flags:
+// warp ballots + popc give each warp its active-row count, one CTA-wide
+// exclusive scan turns counts into positions.  The whole decision of
+// _sparse_out_proj (density = n_active/M, dense when density > 0.5) is made
+// on the device, so the host never waits for it.
+#include "nt_kernels.cuh"
+
+#include <algorithm>
+
+namespace nt {
+
+// ---------------------------------------------------------------------------
+// RMSNorm: y = rnd(rnd(x * 1/sqrt(mean(x^2) + eps)) * w), eps = FLT_EPSILON.
+// torch computes rms_norm in float32 for bf16 inputs and rounds the
+// normalised value to the input dtype before the weight multiply.
+// One warp per row.
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(int64_t M, int64_t D, const void* xv, const void* wv, void* yv) {
+    using E = Elem<DT>;
+    using T = typename E::T;
+    const T* x = static_cast<const T*>(xv);
+    const T* w = static_cast<const T*>(wv);
+    T* y = static_cast<T*>(yv);
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
+        const T* xr = x + r * D;
+        float ss = 0.f;
+        for (int64_t i = lane; i < D; i += 32) {
+            const float v = E::load(xr + i);
+            ss = fmaf(v, v, ss);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float mean = ss / (float)D;
+        const float rs = 1.0f / sqrtf(mean + 1.1920928955078125e-07f);
+        T* yr = y + r * D;
+        for (int64_t i = lane; i < D; i += 32) {
+            const float v = E::rnd(E::load(xr + i) * rs);
+            yr[i] = E::from_f(v * E::load(w + i));
+        }
+    }
+}
+
+int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w, void* y, cudaStream_t stream) {
+    const int64_t blocks = std::min<int64_t>((M + 7) / 8, 148 * 16);
+    if (dtype == NT_F32) rmsnorm_kernel<NT_F32><<<(unsigned)blocks, 256, 0, stream>>>(M, D, x, w, y);
+    else if (dtype == NT_BF16) rmsnorm_kernel<NT_BF16><<<(unsigned)blocks, 256, 0, stream>>>(M, D, x, w, y);
+    else return fail(NT_ERR_DTYPE, "rmsnorm: dtype %d", dtype);
+    return check_launch("rmsnorm_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// flags[r] = any(spikes[r, :] != 0).  One warp per row, 16-byte loads when
+// the row is 16-byte aligned; a value is non-zero when its magnitude bits
+// are (so -0.0 counts as zero, as in torch's `any`).
+// ---------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) row_any_kernel(int64_t M, int64_t K, const void* sv, unsigned char* flags) {
+    using T = typename Elem<DT>::T;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t row_bytes = K * (int64_t)sizeof(T);
+    const bool vec = (row_bytes % 16 == 0) && ((reinterpret_cast<uintptr_t>(sv) & 15) == 0);
+    const uint32_t mag = sizeof(T) == 2 ? 0x7FFF7FFFu : 0x7FFFFFFFu;
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
+        uint32_t acc = 0;
+        if (vec) {
+            const uint4* p = reinterpret_cast<const uint4*>(static_cast<const char*>(sv) + r * row_bytes);
+            const int64_t nv = row_bytes / 16;
+            for (int64_t i = lane; i < nv; i += 32) {
+                const uint4 q = __ldg(p + i);
+                acc |= (q.x | q.y | q.z | q.w) & mag;
+            }
+        } else {
+            const T* p = static_cast<const T*>(sv) + r * K;
+            for (int64_t i = lane; i < K; i += 32) acc |= (Elem<DT>::load(p + i) != 0.f) ? 1u : 0u;
+        }
+        const unsigned any = __ballot_sync(0xffffffffu, acc != 0);
+        if (lane == 0) flags[r] = any ? 1 : 0;
+    }
+}
+
+int launch_row_any(int dtype, int64_t M, int64_t K, const void* spikes, unsigned char* flags, cudaStream_t stream) {
+    const int64_t blocks = std::min<int64_t>((M + 7) / 8, 148 * 16);
+    if (dtype == NT_F32) row_any_kernel<NT_F32><<<(unsigned)blocks, 256, 0, stream>>>(M, K, spikes, flags);
+    else if (dtype == NT_BF16) row_any_kernel<NT_BF16><<<(unsigned)blocks, 256, 0, stream>>>(M, K, spikes, flags);
+    else return fail(NT_ERR_DTYPE, "row_any: dtype %d", dtype);
+    return check_launch("row_any_kernel");
+}
+
+__global__ void __launch_bounds__(256) row_any_partials_kernel(int64_t M, int64_t n, const unsigned short* p, unsigned char* flags) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M; r += (int64_t)gridDim.x * blockDim.x) {
+        unsigned acc = 0;
+        for (int64_t j = 0; j < n; ++j) acc |= p[r * n + j];
+        flags[r] = acc ? 1 : 0;
+    }
+}
+
+int launch_row_any_partials(int64_t M, int64_t n_cblk, const unsigned short* partials, unsigned char* flags,
+                            cudaStream_t stream) {
+    const int64_t blocks = std::min<int64_t>((M + 255) / 256, 148 * 8);
+    row_any_partials_kernel<<<(unsigned)blocks, 256, 0, stream>>>(M, n_cblk, partials, flags);
+    return check_launch("row_any_partials_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Single-CTA stream compaction.  counters[0] = n_active, counters[1] = 1 when
+// the sparse branch is taken, counters[2] = rows the out_proj GEMM processes
+// (n_active when sparse, M when dense).  row_idx lists those rows; row_pos
+// maps a row to its compacted position (-1 when skipped).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) compact_rows_kernel(int64_t M, const unsigned char* flags, int* row_pos,
+                                                            int* row_idx, int* counters, long long* n_active_out,
+                                                            int sparse_enabled) {
+    __shared__ int warp_tot[32];
+    __shared__ int s_total;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t per = (M + 1023) / 1024;
+    const int64_t r0 = tid * per, r1 = (r0 + per < M) ? r0 + per : M;
+    int cnt = 0;
+    for (int64_t r = r0; r < r1; ++r) cnt += flags[r] ? 1 : 0;
+    // inclusive scan of cnt across the CTA
+    int v = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += o;
+    }
+    if (lane == 31) warp_tot[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        int w = warp_tot[lane];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, w, off);
+            if (lane >= off) w += o;
+        }
+        warp_tot[lane] = w;            // inclusive
+        if (lane == 31) s_total = w;
+    }
+    __syncthreads();
+    const int n_active = s_total;
+    const bool sparse = sparse_enabled && (2LL * n_active <= M);
+    int pos = v - cnt + (warp ? warp_tot[warp - 1] : 0);   // exclusive prefix
+    if (sparse) {
+        for (int64_t r = r0; r < r1; ++r) {
+            if (flags[r]) { row_pos[r] = pos; row_idx[pos] = (int)r; ++pos; }
+            else row_pos[r] = -1;
+        }
+    } else {
+        for (int64_t r = r0; r < r1; ++r) { row_pos[r] = (int)r; row_idx[r] = (int)r; }
+    }
+    if (tid == 0) {
+        counters[0] = n_active;
+        counters[1] = sparse ? 1 : 0;
+        counters[2] = sparse ? n_active : (int)M;
+        if (n_active_out) *n_active_out = n_active;
+    }
+}
+
+int launch_compact_rows(int64_t M, const unsigned char* flags, int* row_pos, int* row_idx, int* counters,
+                        long long* n_active_out, int sparse_enabled, cudaStream_t stream) {
+    if (M > (int64_t)INT32_MAX) return fail(NT_ERR_ARG, "compact_rows: M too large");
+    compact_rows_kernel<<<1, 1024, 0, stream>>>(M, flags, row_pos, row_idx, counters, n_active_out, sparse_enabled);
+    return check_launch("compact_rows_kernel");
+}
+
+// dst[i, :] = src[row_idx[i], :] for i < counters[2].  Rows of 16-byte chunks.
+__global__ void __launch_bounds__(256) gather_rows_kernel(int64_t M, int64_t row_bytes, const char* src,
+                                                          const int* row_idx, const int* counters, char* dst) {
+    const int64_t m = counters[2];
+    const int64_t chunks = row_bytes / 16;
+    const int64_t total = m * chunks;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / chunks, k = i % chunks;
+        const int64_t sr = row_idx[r];
+        reinterpret_cast<uint4*>(dst + r * row_bytes)[k] = __ldg(reinterpret_cast<const uint4*>(src + sr * row_bytes) + k);
+    }
+}
+
+int launch_gather_rows(int dtype, int64_t M, int64_t K, const void* src, const int* row_idx, const int* counters,
+                       void* dst, cudaStream_t stream) {
+    const int64_t es = dtype == NT_F32 ? 4 : 2;
+    const int64_t row_bytes = K * es;
+    if (row_bytes % 16) return fail(NT_ERR_ARG, "gather_rows: row bytes %lld not a multiple of 16", (long long)row_bytes);
+    const int64_t blocks = std::min<int64_t>((M * (row_bytes / 16) + 255) / 256, 148 * 16);
+    gather_rows_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
+        M, row_bytes, static_cast<const char*>(src), row_idx, counters, static_cast<char*>(dst));
+    return check_launch("gather_rows_kernel");
+}
+
+// For rows skipped by the sparse branch (row_pos[r] < 0 and counters[1] != 0):
+// dst[r, :] = src ? src[r, :] : 0.
+template <typename T>
+__global__ void __launch_bounds__(256) fill_inactive_kernel(int64_t M, int64_t N, const int* row_pos,
+                                                            const int* counters, const T* src, T* dst) {
+    if (counters[1] == 0) return;
+    const int64_t total = M * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / N;
+        if (row_pos[r] >= 0) continue;
+        dst[i] = src ? src[i] : T(0.f);
+    }
+}
+
+int launch_fill_inactive(int dtype, int64_t M, int64_t N, const int* row_pos, const int* counters,
+                         const void* src, void* dst, cudaStream_t stream) {
+    const int64_t blocks = std::min<int64_t>((M * N + 255) / 256, 148 * 16);
+    if (dtype == NT_F32)
+        fill_inactive_kernel<float><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
+            M, N, row_pos, counters, static_cast<const float*>(src), static_cast<float*>(dst));
+    else
+        fill_inactive_kernel<__nv_bfloat16><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
+            M, N, row_pos, counters, static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst));
+    return check_launch("fill_inactive_kernel");
+}
+
+}  // namespace nt

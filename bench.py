@@ -1,0 +1,341 @@
+"""Benchmark: small-preset bf16 prefill (B=8 per GPU, L=2048) through the B200 kernels.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one ``NeuraTensorModel`` forward (12 FusedSpikeBlocks, 2 sliding-
+window attention layers, tied lm_head) over a [8, 2048] batch of uniform
+random token ids, with the per-layer spike metrics read back.  Weights are
+random-init from a seed.  With N GPUs (torchrun) every rank runs its own
+batch of 8 sequences (sequences are independent: weak scaling, no collective
+on the data path); NCCL only gathers the per-rank spike counts.
+
+Printed JSON (rank 0): ``value`` = tokens/s over all ranks with inputs
+already in HBM, timed with CUDA events per step (max over ranks), L2 flushed
+between timed steps; ``e2e`` = the same through ``InferenceEngine.run`` with
+the ids copied from pinned host memory and the metrics read back each step;
+``roofline`` = the selective-scan kernel on one layer of this workload;
+``cpu_baseline`` = the CPU oracle port on a bounded sample of the workload.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle port of NeuraTensor's PyTorch path; the reference itself is not
+available on the GPU host) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PRESET = "small"
+BATCH = 8
+SEQ = 2048
+SEED = 1234
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler running while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"nt_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
+        except Exception:
+            rows = []
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(budget_s: float = 20.0):
+    """CPU oracle port of the reference path on a bounded sample: small preset bf16, B=1, T=128."""
+    import numpy as np
+    import torch
+    from neuratensor_b200 import NeuraTensorModel, get_preset
+    from oracle import neuratensor_oracle as O
+    torch.manual_seed(SEED)
+    m = NeuraTensorModel(get_preset(PRESET))
+    p = O.params_from_state_dict(m.state_dict())
+    for k in p:
+        p[k] = O.bf16(p[k])
+    c = m.config
+    cfg = O.OracleConfig(vocab_size=c.vocab_size, d_model=c.d_model, n_layers=c.n_layers, d_state=c.d_state,
+                         max_seq_len=c.max_seq_len, attn_every=c.attn_every, attn_heads=c.attn_heads,
+                         attn_window=c.attn_window)
+    rng = np.random.default_rng(SEED)
+    T_sample = 128
+    toks, t0 = 0, time.perf_counter()
+    while True:
+        ids = rng.integers(0, c.vocab_size, (1, T_sample))
+        O.model_forward(ids, p, cfg, None, "bf16")
+        toks += T_sample
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": toks / dt, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"oracle (numpy, bf16-rounding emulation) small preset, B=1 x T={T_sample}, "
+                      f"{toks // T_sample} forwards in {dt:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    from neuratensor_b200 import NeuraTensorModel, get_preset
+    from oracle import neuratensor_oracle as O
+    torch.manual_seed(SEED)
+    m = NeuraTensorModel(get_preset(PRESET))
+    p = O.params_from_state_dict(m.state_dict())
+    for k in p:
+        p[k] = O.bf16(p[k])
+    c = m.config
+    cfg = O.OracleConfig(vocab_size=c.vocab_size, d_model=c.d_model, n_layers=c.n_layers, d_state=c.d_state,
+                         max_seq_len=c.max_seq_len, attn_every=c.attn_every, attn_heads=c.attn_heads,
+                         attn_window=c.attn_window)
+    rng = np.random.default_rng(SEED)
+    T_sample = 64
+    for _ in range(args.warmup):
+        O.model_forward(rng.integers(0, c.vocab_size, (1, T_sample)), p, cfg, None, "bf16")
+    times = []
+    for _ in range(args.steps):
+        ids = rng.integers(0, c.vocab_size, (1, T_sample))
+        t0 = time.perf_counter()
+        O.model_forward(ids, p, cfg, None, "bf16")
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    v = T_sample * args.steps / tot
+    cores = os.cpu_count() or 1
+    line = {"metric": "tokens/s", "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "small preset bf16 prefill (sampled: B=1 x T=64 per step on host cores)",
+                       "preset": PRESET, "seq_len_sample": T_sample},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"oracle port of the reference PyTorch path, B=1 x T={T_sample} per step"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def scan_roofline(model, ids, dev, peak_gbs, peak_kind, reps=20):
+    """Time the selective-scan kernel on one layer of this workload with CUDA events."""
+    import torch
+    from neuratensor_b200 import native
+    blk = model.blocks[0]
+    w, _ = blk._native_weights(torch.bfloat16, dev)
+    with torch.no_grad():
+        x = model.embedding(ids)
+        h, gate = native.rmsnorm_in_proj(x, w["norm_w"], w["W_in"])
+        spk, _ = native.lif_scan(h, w["beta"], w["threshold"])
+        Wp = w["W_proj"]
+        di = h.shape[-1]
+        N = w["log_A"].shape[-1]
+        proj = torch.nn.functional.linear(spk, Wp)
+        dt = torch.nn.functional.softplus(proj[..., :di] + w["b_dt"]).contiguous()
+        Bm = proj[..., di:di + N].contiguous()
+        Cm = proj[..., di + N:].contiguous()
+        st = torch.zeros(x.shape[0], di, N, dtype=torch.bfloat16, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        for _ in range(3):
+            native.selective_scan(spk, dt, Bm, Cm, w["log_A"], w["D"], st, gate=gate)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        ms = 0.0
+        for a, b in ev:
+            flush.zero_()
+            a.record(stream)
+            native.selective_scan(spk, dt, Bm, Cm, w["log_A"], w["D"], st, gate=gate)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = sum(a.elapsed_time(b) for a, b in ev) / reps
+    B, T = ids.shape
+    M = B * T
+    es = 2
+    algo = M * di * es * 4 + M * 2 * N * es + 2 * B * di * N * es   # u, dt, gate, o + B|C + state in/out
+    achieved = algo / (ms * 1e-3) / 1e9
+    return {"kernel": "scan_kernel (selective scan + gate, one layer)", "bound": "hbm", "achieved": achieved,
+            "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs, "traffic": None,
+            "algorithmic_bytes": algo, "ms_per_launch": ms, "peak_source": peak_kind}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    from neuratensor_b200 import InferenceEngine, NeuraTensorModel, get_preset
+    from neuratensor_b200.native import load
+    load()
+    torch.manual_seed(SEED)
+    model = NeuraTensorModel(get_preset(PRESET))
+    eng = InferenceEngine(model, device=f"cuda:{local}", dtype=torch.bfloat16)
+    model = eng.model
+    g = torch.Generator().manual_seed(SEED + rank)
+    host_ids = [torch.randint(0, model.config.vocab_size, (BATCH, SEQ), generator=g).pin_memory()
+                for _ in range(2)]
+    dev_ids = [h.to(dev) for h in host_ids]
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step(i):
+        logits, _, counts = model.forward_device(dev_ids[i % 2])
+        return counts
+
+    with torch.no_grad():
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        counts = None
+        with Clocks(local) as clk:
+            torch.cuda.synchronize(dev)
+            for i, (a, b) in enumerate(evs):
+                flush.zero_()
+                a.record(stream)
+                counts = step(i)
+                b.record(stream)
+            torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        ms = sum(a.elapsed_time(b) for a, b in evs)
+        clocks = clk.summary()
+
+        # spike metrics: NCCL gather of per-rank per-layer counts (off the timed path)
+        if world > 1:
+            allc = [torch.zeros_like(counts) for _ in range(world)]
+            dist.all_gather(allc, counts)
+            tot = torch.stack(allc).sum(0)
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        else:
+            tot = counts
+        di = model.config.d_model * model.config.expand
+        metrics = model.metrics_from_counts(tot.tolist(), BATCH * SEQ * di * world, torch.bfloat16)
+
+        # end to end through the public API: pinned host ids -> run() -> metrics on the host
+        e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+        for i in range(2):
+            eng.run(host_ids[i % 2], reset_state=True)
+        if world > 1:
+            dist.barrier()
+        for i, (a, b) in enumerate(e2e_ev):
+            flush.zero_()
+            a.record(stream)
+            r = eng.run(host_ids[i % 2], reset_state=True)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+
+        roof = None
+        if rank == 0:
+            peak, kind = _peaks()
+            roof = scan_roofline(model, dev_ids[0], dev, peak, kind)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    tokens = BATCH * SEQ * world * args.steps
+    value = tokens / (ms / 1000.0)
+    e2e_value = tokens / (e2e_ms / 1000.0)
+    launches_per_step = 9 * model.config.n_layers
+    cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
+    line = {
+        "metric": "tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random ids, random-init weights, seeded)",
+        "config": {"workload": f"small preset bf16 prefill, B={BATCH} per GPU x L={SEQ}", "preset": PRESET,
+                   "global_batch": BATCH * world, "seq_len": SEQ, "parallelism": f"dp{world} (batch shards)",
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * SEQ * 8,
+                "d2h_bytes_per_step": 8 * model.config.n_layers},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+        "spike_rate": metrics["spike_rate"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -60,8 +60,9 @@ __device__ __forceinline__ float ex2(float x) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Bounded spin limits.  Every wait in these kernels gives up after this many
-// polls, raises a flag in the device error word and lets the kernel finish.
-constexpr uint32_t kSpinLimit = 1u << 26;
+// Bounded waits.  Every mbarrier wait in these kernels gives up after this
+// much wall time (read from %globaltimer), raises a flag in the device error
+// word and lets the kernel finish; no launch here runs for more than a few ms.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 }  // namespace nt

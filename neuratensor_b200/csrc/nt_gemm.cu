@@ -74,11 +74,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
 }
-// Bounded wait: false when the limit expired.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: false when kWaitLimitNs of wall time passed without the phase completing.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < (kSpinLimit >> 2); ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
     asm volatile(
@@ -220,8 +229,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         // ---------------- epilogue: TMEM -> registers -> global ----------------
         const int q = warp & 3;                     // TMEM lane quarter this warp may access
         const int64_t row = m0 + q * 32 + lane;
-        if (!mbar_wait(smem_u32(&S.acc), 0)) {
-            atomicOr(err, ERRF_TIMEOUT_EPILOGUE);
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&S.acc), 0));
+        __syncwarp();                               // tcgen05.ld is .sync.aligned: whole warp, converged
+        if (!ok) {
+            if (lane == 0) atomicOr(err, ERRF_TIMEOUT_EPILOGUE);
         } else {
             tc_fence_after();
 #pragma unroll 1
@@ -241,6 +252,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
+        __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
     }

@@ -68,7 +68,7 @@ lif_scan_kernel(LifArgs a) {
             }
             if (live) sp[t * a.s_st] = E::from_f(spk);
             const unsigned ballot = __ballot_sync(0xffffffffu, live && spk != 0.f);
-            local_count += (spk != 0.f) ? 1u : 0u;
+            local_count += (live && spk != 0.f) ? 1u : 0u;
             if (a.row_partials) {
                 const int r = (int)(t % ROWS);
                 if (lane == 0) row_cnt[r][warp] = (unsigned short)__popc(ballot);

@@ -4,22 +4,34 @@
 //
 // Work split: a channel's d_state recurrences are spread over TPC threads
 // (8 states each, TPC = next power of two >= N/8), so a 128-thread CTA owns
-// CPB = 128/TPC channels of one batch row.  Time is walked serially in
-// chunks of TCH steps: each chunk's inputs (u, dt, gate, B, C) are staged in
-// shared memory with coalesced loads, the recurrence runs from registers, and
-// the chunk's outputs are written back coalesced.  The state never leaves
-// registers between chunks; it is float32 whatever the activation dtype.
+// CPB = 128/TPC channels of one batch row and walks time serially.
 //
-// Discretisation per step (A = -exp(log_A), computed once per state):
-//   A_bar = exp(dt*A)             -> ex2(dt * A*log2(e)) on the MUFU pipe
-//   B_bar = (A_bar - 1)/A * B     (dt*B where |A| < 1e-6, ssm.py:129-137)
-//   h     = A_bar*h + B_bar*u     (the B_bar term is skipped when u == 0)
+// Per chunk of TCH steps:
+//   1. cp.async stages the next chunk's raw inputs (u or x, dt, gate, B, C)
+//      into shared memory while the current chunk computes (double buffer);
+//   2. the chunk is widened once to float32 work buffers;
+//   3. each thread advances its 8 states through TCH steps from registers
+//      (packed f32x2 arithmetic) and writes one partial C.h sum per step to
+//      shared memory -- no shuffles on the serial path;
+//   4. partial sums are reduced per (step, channel), D*u and the gate are
+//      applied, and the chunk is stored with coalesced writes.
+// The state is float32 in registers for the whole sequence.
+//
+// Discretisation per step (A = -exp(log_A)):
+//   A_bar = exp(dt*A)            -> ex2(dt * A*log2(e)) on the MUFU pipe
+//   B_bar = (A_bar - 1)/A * B    (dt*B where |A| < 1e-6, ssm.py:129-137)
+//   h     = A_bar*h + B_bar*u    (the B_bar term is skipped when u == 0)
 //   y     = sum_n C[n]*h[n] + D*u
-// When A has the HiPPO structure A[c,n] = (n+1)*A[c,0] (the reference's
-// initialisation, ssm.py:34-43) the kernel detects it per CTA and replaces
-// the per-state exponentials by one exponential per thread and a chain of
-// multiplies: exp(dt*A[c,n+1]) = exp(dt*A[c,n]) * exp(dt*A[c,0]).
+// HiPPO fast path: when A[c,n] = (n+1)*A[c,0] for every state of every
+// channel of the CTA (the reference's initialisation, ssm.py:34-43), a
+// thread needs two exponentials per step and a chain of multiplies:
+// exp(dt*A[c,n+1]) = exp(dt*A[c,n]) * exp(dt*A[c,0]).  The structure test is
+// 1e-6 relative for float32 parameters and 2 bf16 ulps for bfloat16 ones
+// (a bf16 model stores log(n+1) rounded, so exp(log_A) lands within an ulp or
+// two of n+1); on the fast path A is exactly (n+1)*A[c,0].
 #include "nt_kernels.cuh"
+
+#include <type_traits>
 
 namespace nt {
 
@@ -28,49 +40,99 @@ namespace {
 constexpr int kTch = 32;    // time steps per staged chunk
 constexpr int kNpt = 8;     // d_state entries per thread
 
-template <int DT>
-__device__ __forceinline__ float ld_act(const void* p, int64_t i) {
-    return Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(p) + i);
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
 
-// MODE 0: plain selective scan (u given).  MODE 1: u = LIF spikes of x.
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Stage rows [t0, t0+TCH) x [col0, col0+NCOLS) of a row-major matrix (leading
+// dimension ld elements) into smem rows of NCOLS elements.  16-byte cp.async
+// copies when the whole tile is aligned, element copies (zero fill outside
+// the matrix) otherwise.
+template <typename T, int NCOLS>
+__device__ __forceinline__ void stage_tile(T* dst, const T* src, int64_t ld, int64_t t0, int64_t T_len,
+                                           int64_t col0, int64_t col_lim, bool vec_ok, int tid) {
+    constexpr int EPV = 16 / (int)sizeof(T);      // elements per 16-byte vector
+    if constexpr (NCOLS % EPV == 0) {
+        if (vec_ok) {
+            constexpr int VPR = NCOLS / EPV;        // vectors per row
+            for (int i = tid; i < kTch * VPR; i += 128) {
+                const int tt = i / VPR, v = i % VPR;
+                const int64_t t = t0 + tt;
+                T* dp = dst + tt * NCOLS + v * EPV;
+                if (t < T_len) cp_async16(dp, src + t * ld + col0 + v * EPV);
+                else *reinterpret_cast<uint4*>(dp) = make_uint4(0, 0, 0, 0);
+            }
+            return;
+        }
+    }
+    {
+        for (int i = tid; i < kTch * NCOLS; i += 128) {
+            const int tt = i / NCOLS, cc = i % NCOLS;
+            const int64_t t = t0 + tt, cidx = col0 + cc;
+            dst[i] = (t < T_len && cidx < col_lim) ? src[t * ld + cidx] : T(0.f);
+        }
+    }
+}
+
+template <int TPC, typename T>
+struct ScanSmem {
+    static constexpr int CPB = 128 / TPC;
+    static constexpr int NP = kNpt * TPC;
+    static constexpr int RAW = 3 * kTch * CPB + 2 * kTch * NP;       // elements of T per staging buffer
+    static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
+    static constexpr int WORK_FLOATS = 2 * kTch * CPB + 2 * kTch * NP + kTch * 128 + kTch * CPB;
+    static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + sizeof(float) * (size_t)WORK_FLOATS;
+};
+
+// MODE 0: selective scan with given u.  MODE 1: u = LIF spikes of x (fused op).
 template <int DT, int SDT, int TPC, int MODE>
 __global__ void __launch_bounds__(128)
 scan_kernel(ScanArgs a, FusedArgs f) {
-    constexpr int CPB = 128 / TPC;
-    constexpr int NP = kNpt * TPC;
-    extern __shared__ float smem[];
-    float* s_u = smem;                 // [kTch][CPB]  u (MODE 0) or x (MODE 1)
-    float* s_dt = s_u + kTch * CPB;    // [kTch][CPB]
-    float* s_g = s_dt + kTch * CPB;    // [kTch][CPB]  gate
-    float* s_y = s_g + kTch * CPB;     // [kTch][CPB]  y (and spikes in MODE 1 via s_g)
-    float* s_B = s_y + kTch * CPB;     // [kTch][NP]
-    float* s_C = s_B + kTch * NP;      // [kTch][NP]
+    using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
+    using L = ScanSmem<TPC, T>;
+    constexpr int CPB = L::CPB, NP = L::NP;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float* w_u = reinterpret_cast<float*>(smem_raw + 2 * L::RAW_BYTES);  // [kTch][CPB] u (or x)
+    float* w_dt = w_u + kTch * CPB;                                      // [kTch][CPB]
+    float* w_B = w_dt + kTch * CPB;                                      // [kTch][NP]
+    float* w_C = w_B + kTch * NP;                                        // [kTch][NP]
+    float* w_yp = w_C + kTch * NP;                                       // [kTch][128] partial C.h
+    float* w_s = w_yp + kTch * 128;                                      // [kTch][CPB] spikes (MODE 1)
 
-    const int64_t T = MODE ? f.L : a.T, d = MODE ? f.d : a.d, N = MODE ? f.N : a.N;
-    const void* p_u = MODE ? f.x : a.u;
-    const void* p_dt = MODE ? f.delta : a.dt;
-    const void* p_B = MODE ? f.Bm : a.Bm;
-    const void* p_C = MODE ? f.Cm : a.Cm;
-    const bool has_gate = (MODE == 0) && a.gate != nullptr;
+    const int64_t T_len = MODE ? f.L : a.T, d = MODE ? f.d : a.d, N = MODE ? f.N : a.N;
+    const T* p_u = static_cast<const T*>(MODE ? f.x : a.u);
+    const T* p_dt = static_cast<const T*>(MODE ? f.delta : a.dt);
+    const T* p_B = static_cast<const T*>(MODE ? f.Bm : a.Bm);
+    const T* p_C = static_cast<const T*>(MODE ? f.Cm : a.Cm);
+    const T* p_g = MODE == 0 ? static_cast<const T*>(a.gate) : nullptr;
+    const bool has_gate = p_g != nullptr;
     const int64_t ld_bc = (MODE == 0 && a.ld_bc > 0) ? a.ld_bc : N;
 
     const int tid = threadIdx.x, cl = tid / TPC, sub = tid % TPC;
     const int64_t c0 = (int64_t)blockIdx.x * CPB, c = c0 + cl, b = blockIdx.y;
     const bool live = c < d;
 
-    // ---- per-state constants ------------------------------------------------
+    // ---- per-state constants -------------------------------------------------
     // A = -exp(log_A), rounded like the reference's own tensor op (ssm.py:121)
     auto load_A = [&](int64_t n) -> float {
-        if (MODE == 0) return -Elem<DT>::rnd(expf(ld_act<DT>(a.log_A, c * N + n)));
+        if (MODE == 0)
+            return -Elem<DT>::rnd(expf(Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.log_A) + c * N + n)));
         return -expf(f.log_A[c * N + n]);
     };
+    const float tol = (MODE == 0 && DT == NT_BF16) ? 7.8125e-3f : 1e-6f;
     float A2[kNpt], cinv[kNpt], h[kNpt];
     unsigned lim_mask = 0;
     bool hippo_ok = true;
-    const float Abase = live ? load_A(0) : 0.f;
+    const float Abase = live ? load_A(0) : -1.f;
     const void* sin = MODE ? (const void*)f.state_in : a.state_in;
 #pragma unroll
     for (int j = 0; j < kNpt; ++j) {
@@ -81,116 +143,165 @@ scan_kernel(ScanArgs a, FusedArgs f) {
             A = load_A(n);
             if (sin) {
                 const int64_t si = (b * d + c) * N + n;
-                if (MODE == 0 && SDT == NT_BF16) h[j] = ld_act<NT_BF16>(sin, si);
+                if (MODE == 0 && SDT == NT_BF16) h[j] = __bfloat162float(static_cast<const __nv_bfloat16*>(sin)[si]);
                 else h[j] = static_cast<const float*>(sin)[si];
             }
-            // HiPPO structure check: A[c,n] == (n+1) * A[c,0] to 1e-6 relative
-            if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) hippo_ok = false;
+            if (fabsf(A - (float)(n + 1) * Abase) > tol * fabsf(A)) hippo_ok = false;
         }
-        A2[j] = A * kLog2e;
         const bool lim = (live && n < N) && fabsf(A) < 1e-6f;
         if (lim) { lim_mask |= 1u << j; hippo_ok = false; }
+        A2[j] = A * kLog2e;
         cinv[j] = (A == 0.f) ? 0.f : 1.0f / A;
     }
-    const float q2 = Abase * kLog2e;
     const bool hippo = __syncthreads_and(hippo_ok ? 1 : 0) != 0;
-    float Dv = 0.f, beta = 0.f, th = 0.f, mem = 0.f;
-    if (live) {
-        Dv = MODE == 0 ? ld_act<DT>(a.D, c) : f.Dskip[c];
-        if (MODE == 1) {
-            beta = f.beta[c];
-            th = f.threshold[c];
-            if (f.mem_in) mem = f.mem_in[b * d + c];
+    if (hippo) {
+        // exact HiPPO structure on the fast path: A[c,n] = (n+1) * A[c,0]
+#pragma unroll
+        for (int j = 0; j < kNpt; ++j) {
+            const float A = (float)(sub * kNpt + j + 1) * Abase;
+            A2[j] = A * kLog2e;
+            cinv[j] = 1.0f / A;
         }
+    }
+    const float q2 = Abase * kLog2e;
+    float beta = 0.f, th = 0.f, mem = 0.f;
+    if (live && MODE == 1) {
+        beta = f.beta[c];
+        th = f.threshold[c];
+        if (f.mem_in) mem = f.mem_in[b * d + c];
     }
     unsigned spike_local = 0;
     const bool sparse_rows = (MODE == 0) && a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
 
-    for (int64_t t0 = 0; t0 < T; t0 += kTch) {
+    // 16-byte staging is possible when every tile row starts 16-byte aligned
+    constexpr int EPV = 16 / (int)sizeof(T);
+    const bool act_vec = (d % EPV == 0) && (c0 + CPB <= d) &&
+                         ((reinterpret_cast<uintptr_t>(p_u) | reinterpret_cast<uintptr_t>(p_dt) |
+                           reinterpret_cast<uintptr_t>(p_g)) & 15) == 0;
+    const bool bc_vec = (NP == N) && (ld_bc % EPV == 0) &&
+                        ((reinterpret_cast<uintptr_t>(p_B) | reinterpret_cast<uintptr_t>(p_C)) & 15) == 0;
+    const int64_t row0 = b * T_len;   // first (batch, time) row of this batch element
+
+    auto raw_buf = [&](int k) { return reinterpret_cast<T*>(smem_raw + (k & 1) * L::RAW_BYTES); };
+    auto issue = [&](int64_t t0, T* rb) {
+        T* r_u = rb;
+        T* r_dt = r_u + kTch * CPB;
+        T* r_g = r_dt + kTch * CPB;
+        T* r_B = r_g + kTch * CPB;
+        T* r_C = r_B + kTch * NP;
+        stage_tile<T, CPB>(r_u, p_u + row0 * d, d, t0, T_len, c0, d, act_vec, tid);
+        stage_tile<T, CPB>(r_dt, p_dt + row0 * d, d, t0, T_len, c0, d, act_vec, tid);
+        if (has_gate) stage_tile<T, CPB>(r_g, p_g + row0 * d, d, t0, T_len, c0, d, act_vec, tid);
+        stage_tile<T, NP>(r_B, p_B + row0 * ld_bc, ld_bc, t0, T_len, 0, N, bc_vec, tid);
+        stage_tile<T, NP>(r_C, p_C + row0 * ld_bc, ld_bc, t0, T_len, 0, N, bc_vec, tid);
+        cp_async_commit();
+    };
+
+    const int nchunks = (int)((T_len + kTch - 1) / kTch);
+    issue(0, raw_buf(0));
+    for (int k = 0; k < nchunks; ++k) {
+        const int64_t t0 = (int64_t)k * kTch;
+        if (k + 1 < nchunks) {
+            issue(t0 + kTch, raw_buf(k + 1));
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
         __syncthreads();
-        // ---- stage the chunk ----------------------------------------------
+        // ---- widen the chunk to float32 --------------------------------------
+        const T* rb = raw_buf(k);
         for (int i = tid; i < kTch * CPB; i += 128) {
-            const int tt = i / CPB, cc = i % CPB;
-            const int64_t t = t0 + tt, cg = c0 + cc;
-            const bool ok = t < T && cg < d;
-            const int64_t idx = (b * T + t) * d + cg;
-            if (MODE == 0) {
-                s_u[i] = ok ? ld_act<DT>(p_u, idx) : 0.f;
-                s_dt[i] = ok ? ld_act<DT>(p_dt, idx) : 0.f;
-                if (has_gate) s_g[i] = ok ? ld_act<DT>(a.gate, idx) : 0.f;
-            } else {
-                s_u[i] = ok ? ld_act<NT_BF16>(p_u, idx) : 0.f;
-                s_dt[i] = ok ? ld_act<NT_BF16>(p_dt, idx) : 0.f;
-            }
+            w_u[i] = to_f(rb[i]);
+            w_dt[i] = to_f(rb[kTch * CPB + i]);
         }
         for (int i = tid; i < kTch * NP; i += 128) {
-            const int tt = i / NP, n = i % NP;
-            const int64_t t = t0 + tt;
-            const bool ok = t < T && n < N;
-            const int64_t idx = (b * T + t) * ld_bc + n;
-            s_B[i] = ok ? (MODE == 0 ? ld_act<DT>(p_B, idx) : ld_act<NT_BF16>(p_B, idx)) : 0.f;
-            s_C[i] = ok ? (MODE == 0 ? ld_act<DT>(p_C, idx) : ld_act<NT_BF16>(p_C, idx)) : 0.f;
+            w_B[i] = to_f(rb[3 * kTch * CPB + i]);
+            w_C[i] = to_f(rb[3 * kTch * CPB + kTch * NP + i]);
         }
         __syncthreads();
-        const int nt = (T - t0 < kTch) ? (int)(T - t0) : kTch;
-        for (int tt = 0; tt < nt; ++tt) {
+        // ---- recurrence ------------------------------------------------------
+        const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
+        auto step = [&](int tt, auto hip) {
+            constexpr bool HIP = decltype(hip)::value;
             float u;
             if (MODE == 0) {
-                u = s_u[tt * CPB + cl];
+                u = w_u[tt * CPB + cl];
             } else {
-                // LIF step (snn.py:177-181) in fp32, same in every thread of the channel
-                mem = __fadd_rn(__fmul_rn(beta, mem), s_u[tt * CPB + cl]);
+                // LIF step (snn.py:177-181) in fp32, identical in every thread of the channel
+                mem = __fadd_rn(__fmul_rn(beta, mem), w_u[tt * CPB + cl]);
                 u = (mem >= th) ? 1.f : 0.f;
                 mem = __fsub_rn(mem, __fmul_rn(th, u));
             }
-            const float dtv = s_dt[tt * CPB + cl];
-            float av[kNpt];
-            if (hippo) {
-                av[0] = ex2(dtv * A2[0]);
+            const float dtv = w_dt[tt * CPB + cl];
+            float2 av[kNpt / 2];
+            if (HIP) {
+                const float a0 = ex2(dtv * A2[0]);
                 const float qv = ex2(dtv * q2);
+                av[0] = make_float2(a0, a0 * qv);
+                const float q_sq = qv * qv;
+                const float2 qq = make_float2(q_sq, q_sq);
 #pragma unroll
-                for (int j = 1; j < kNpt; ++j) av[j] = av[j - 1] * qv;
+                for (int j = 1; j < kNpt / 2; ++j) av[j] = __fmul2_rn(av[j - 1], qq);
             } else {
 #pragma unroll
-                for (int j = 0; j < kNpt; ++j) av[j] = ex2(dtv * A2[j]);
+                for (int j = 0; j < kNpt / 2; ++j) av[j] = make_float2(ex2(dtv * A2[2 * j]), ex2(dtv * A2[2 * j + 1]));
             }
-            const float4* Bp = reinterpret_cast<const float4*>(s_B + tt * NP + sub * kNpt);
-            const float4* Cp = reinterpret_cast<const float4*>(s_C + tt * NP + sub * kNpt);
+            const float4* Bp = reinterpret_cast<const float4*>(w_B + tt * NP + sub * kNpt);
+            const float4* Cp = reinterpret_cast<const float4*>(w_C + tt * NP + sub * kNpt);
             const float4 b0 = Bp[0], b1 = Bp[1], k0 = Cp[0], k1 = Cp[1];
-            const float Bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-            const float Cv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+            const float2 Bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                  make_float2(b1.z, b1.w)};
+            const float2 Cv[4] = {make_float2(k0.x, k0.y), make_float2(k0.z, k0.w), make_float2(k1.x, k1.y),
+                                  make_float2(k1.z, k1.w)};
+            float2 hv[4] = {make_float2(h[0], h[1]), make_float2(h[2], h[3]), make_float2(h[4], h[5]),
+                            make_float2(h[6], h[7])};
             if (u != 0.f) {
+                const float2 uu = make_float2(u, u);
 #pragma unroll
-                for (int j = 0; j < kNpt; ++j) {
-                    const float coef = (lim_mask >> j & 1u) ? dtv : (av[j] - 1.0f) * cinv[j];
-                    h[j] = fmaf(av[j], h[j], coef * Bv[j] * u);
+                for (int j = 0; j < kNpt / 2; ++j) {
+                    float2 coef;
+                    coef.x = ((lim_mask >> (2 * j)) & 1u) ? dtv : (av[j].x - 1.0f) * cinv[2 * j];
+                    coef.y = ((lim_mask >> (2 * j + 1)) & 1u) ? dtv : (av[j].y - 1.0f) * cinv[2 * j + 1];
+                    const float2 bu = __fmul2_rn(__fmul2_rn(coef, Bv[j]), uu);
+                    hv[j] = __ffma2_rn(av[j], hv[j], bu);
                 }
             } else {
 #pragma unroll
-                for (int j = 0; j < kNpt; ++j) h[j] = av[j] * h[j];
+                for (int j = 0; j < kNpt / 2; ++j) hv[j] = __fmul2_rn(av[j], hv[j]);
             }
-            float yp = 0.f;
 #pragma unroll
-            for (int j = 0; j < kNpt; ++j) yp = fmaf(Cv[j], h[j], yp);
-#pragma unroll
-            for (int off = TPC / 2; off > 0; off >>= 1) yp += __shfl_xor_sync(0xffffffffu, yp, off);
-            if (sub == 0) {
-                s_y[tt * CPB + cl] = __fadd_rn(yp, __fmul_rn(Dv, u));
-                if (MODE == 1) s_g[tt * CPB + cl] = u;
-            }
-            if (MODE == 1 && sub == 0 && live) spike_local += (u != 0.f);
+            for (int j = 0; j < kNpt / 2; ++j) { h[2 * j] = hv[j].x; h[2 * j + 1] = hv[j].y; }
+            float2 y0 = __fmul2_rn(Cv[0], hv[0]);
+            float2 y1 = __fmul2_rn(Cv[1], hv[1]);
+            y0 = __ffma2_rn(Cv[2], hv[2], y0);
+            y1 = __ffma2_rn(Cv[3], hv[3], y1);
+            w_yp[tt * 128 + tid] = (y0.x + y0.y) + (y1.x + y1.y);
+            if (MODE == 1 && sub == 0) w_s[tt * CPB + cl] = u;
+        };
+        if (hippo) {
+#pragma unroll 4
+            for (int tt = 0; tt < nt; ++tt) step(tt, std::true_type{});
+        } else {
+#pragma unroll 4
+            for (int tt = 0; tt < nt; ++tt) step(tt, std::false_type{});
         }
         __syncthreads();
-        // ---- write the chunk's outputs -------------------------------------
+        // ---- reduce partial sums, D*u, gate; coalesced stores -----------------
         for (int i = tid; i < kTch * CPB; i += 128) {
             const int tt = i / CPB, cc = i % CPB;
             const int64_t t = t0 + tt, cg = c0 + cc;
-            if (t >= T || cg >= d) continue;
-            int64_t row = b * T + t;
+            if (tt >= nt || cg >= d) continue;
+            float yp = 0.f;
+#pragma unroll
+            for (int s2 = 0; s2 < TPC; ++s2) yp += w_yp[tt * 128 + cc * TPC + s2];
+            const float uu = MODE == 0 ? w_u[i] : w_s[i];
+            const float Dc = MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + cg) : f.Dskip[cg];
+            const float yv = __fadd_rn(yp, __fmul_rn(Dc, uu));
+            int64_t row = row0 + t;
             if (MODE == 0) {
                 using E = Elem<DT>;
-                float o = E::rnd(s_y[i]);
-                if (has_gate) o = E::rnd(o * E::rnd(silu_f(s_g[i])));
+                float o = E::rnd(yv);
+                if (has_gate) o = E::rnd(o * E::rnd(silu_f(to_f(rb[2 * kTch * CPB + i]))));
                 if (sparse_rows) {
                     const int pos = a.row_pos[row];
                     if (pos < 0) continue;
@@ -198,15 +309,17 @@ scan_kernel(ScanArgs a, FusedArgs f) {
                 }
                 static_cast<typename E::T*>(a.y)[row * d + cg] = E::from_f(o);
             } else {
-                static_cast<__nv_bfloat16*>(f.y)[row * d + cg] = __float2bfloat16_rn(s_y[i]);
+                static_cast<__nv_bfloat16*>(f.y)[row * d + cg] = __float2bfloat16_rn(yv);
                 if (f.spikes) {
-                    if (f.spike_dtype == NT_U8) static_cast<unsigned char*>(f.spikes)[row * d + cg] = (unsigned char)(s_g[i] != 0.f);
-                    else static_cast<__nv_bfloat16*>(f.spikes)[row * d + cg] = __float2bfloat16_rn(s_g[i]);
+                    if (f.spike_dtype == NT_U8) static_cast<unsigned char*>(f.spikes)[row * d + cg] = (unsigned char)(uu != 0.f);
+                    else static_cast<__nv_bfloat16*>(f.spikes)[row * d + cg] = __float2bfloat16_rn(uu);
                 }
+                spike_local += (uu != 0.f);
             }
         }
+        __syncthreads();   // raw_buf(k) is refilled by the next iteration's issue
     }
-    // ---- carry-out ------------------------------------------------------------
+    // ---- carry-out -----------------------------------------------------------
     void* sout = MODE ? (void*)f.state_out : a.state_out;
     if (live && sout) {
 #pragma unroll
@@ -235,14 +348,13 @@ int pow2_tpc(int64_t N) {
 
 template <int DT, int SDT, int MODE, int TPC>
 int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
-    constexpr int CPB = 128 / TPC;
-    const size_t smem = sizeof(float) * (size_t)(4 * kTch * CPB + 2 * kTch * kNpt * TPC);
+    using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
+    const size_t smem = ScanSmem<TPC, T>::BYTES;
     auto kern = scan_kernel<DT, SDT, TPC, MODE>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
-    }
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
     const int64_t d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
+    constexpr int CPB = 128 / TPC;
     dim3 grid((unsigned)((d + CPB - 1) / CPB), (unsigned)B);
     kern<<<grid, 128, smem, stream>>>(a, f);
     return check_launch("scan_kernel");

@@ -1,0 +1,382 @@
+"""Parity of each C-ABI entry point against the oracle and the golden fixtures (B200).
+
+Tolerances: LIF spikes/membranes are bit-exact (fp32 and the bf16 rounding
+mode); fp32 scan outputs rtol 1e-4 with an atol floor of 1e-6; bf16 outputs
+within 2 bf16 ulps (rtol 2e-2 where a bf16 GEMM precedes).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import gget, golden_params, load_golden, unbits
+from oracle import neuratensor_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def T(a, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(DEV).to(dtype)
+
+
+def N(t):
+    return t.detach().float().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def nat():
+    from neuratensor_b200 import native
+    native.load()
+    return native
+
+
+# --------------------------------------------------------------------------- #
+#  (a) LIF                                                                     #
+# --------------------------------------------------------------------------- #
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+def test_lif_golden_bit_exact(nat, mode):
+    d = load_golden(f"lif_{mode}.npz")
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    x, beta, th, m0 = (T(gget(d, k), dt) for k in ("x", "beta", "theta", "mem0"))
+    spk, mem = nat.lif_scan(x, beta, th, m0)
+    np.testing.assert_array_equal(N(spk), unbits(d["spikes_bits"], d["spikes_shape"]))
+    np.testing.assert_array_equal(N(mem), gget(d, "mem_out"))
+    spk0, mem0 = nat.lif_scan(x, beta, th, None)
+    np.testing.assert_array_equal(N(spk0), unbits(d["spikes_fresh_bits"], d["spikes_shape"]))
+    np.testing.assert_array_equal(N(mem0), gget(d, "mem_out_fresh"))
+    s1, m1 = nat.lif_scan(x[:, :1], beta, th, m0)           # T = 1 (snn.py:64-75)
+    np.testing.assert_array_equal(N(s1)[:, 0], gget(d, "step_spk"))
+    np.testing.assert_array_equal(N(m1), gget(d, "step_mem"))
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("shape", [(1, 1, 1), (2, 65, 129), (3, 300, 333), (1, 2048, 1280)])
+def test_lif_random_bit_exact(nat, mode, shape):
+    rng = np.random.default_rng(7)
+    B, Tn, C = shape
+    x = rng.normal(0.3, 0.8, shape).astype(np.float32)
+    beta = rng.uniform(0.8, 0.99, C).astype(np.float32)
+    th = rng.choice([1.0, 1.5, 2.0], C).astype(np.float32)
+    m0 = rng.normal(0, 0.5, (B, C)).astype(np.float32)
+    if mode == "bf16":
+        x, beta, th, m0 = O.bf16(x), O.bf16(beta), O.bf16(th), O.bf16(m0)
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    count = torch.zeros((), dtype=torch.int64, device=DEV)
+    spk, mem = nat.lif_scan(T(x, dt), T(beta, dt), T(th, dt), T(m0, dt), spike_count=count)
+    rs, rm = O.lif_scan(x, m0, beta, th, mode)
+    np.testing.assert_array_equal(N(spk), rs)
+    np.testing.assert_array_equal(N(mem), rm)
+    assert int(count.item()) == int(rs.sum())
+
+
+def test_lif_strided_input(nat):
+    """LIF on the first half of an in_proj output (row stride 2*C), as in the block."""
+    rng = np.random.default_rng(3)
+    hg = rng.normal(0.2, 1.0, (2, 50, 2 * 96)).astype(np.float32)
+    beta = np.full(96, 0.9, np.float32)
+    th = np.ones(96, np.float32)
+    t = T(hg)
+    spk, mem = nat.lif_scan(t[..., :96], T(beta), T(th))
+    rs, rm = O.lif_scan(hg[..., :96], None, beta, th, "fp32")
+    np.testing.assert_array_equal(N(spk), rs)
+    np.testing.assert_array_equal(N(mem), rm)
+
+
+def test_lif_rejects_bad_args(nat):
+    x = torch.zeros(1, 4, 8, device=DEV)
+    with pytest.raises(ValueError):
+        nat.lif_scan(x, torch.ones(7, device=DEV), torch.ones(8, device=DEV))
+    with pytest.raises(nat.NativeError):
+        nat.lif_scan(torch.zeros(1, 0, 8, device=DEV), torch.ones(8, device=DEV), torch.ones(8, device=DEV))
+    with pytest.raises(RuntimeError):
+        nat.lif_scan(torch.zeros(1, 4, 8), torch.ones(8), torch.ones(8))
+
+
+# --------------------------------------------------------------------------- #
+#  (b) selective scan                                                          #
+# --------------------------------------------------------------------------- #
+
+def _scan_inputs(rng, B, Tn, d, Nst, hippo=True, limit=False):
+    u = (rng.random((B, Tn, d)) < 0.2).astype(np.float32)
+    dt = O.softplus(rng.normal(-2.0, 1.0, (B, Tn, d)).astype(np.float32), "fp32")
+    Bm = (rng.normal(0, 1, (B, Tn, Nst)) / np.sqrt(Nst)).astype(np.float32)
+    Cm = (rng.normal(0, 1, (B, Tn, Nst)) / np.sqrt(Nst)).astype(np.float32)
+    log_A = O.hippo_log_A(d, Nst)
+    if not hippo:
+        log_A = (log_A + rng.normal(0, 0.2, log_A.shape)).astype(np.float32)
+    if limit:
+        log_A[0, 0] = -20.0
+    D = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    st = (rng.normal(0, 0.1, (B, d, Nst))).astype(np.float32)
+    return u, dt, Bm, Cm, log_A, D, st
+
+
+@pytest.mark.parametrize("Nst", [8, 16, 32, 64, 128])
+@pytest.mark.parametrize("hippo", [True, False])
+def test_selective_scan_fp32_vs_oracle(nat, Nst, hippo):
+    rng = np.random.default_rng(Nst + 1000 * hippo)
+    B, Tn, d = 2, 97, 72
+    u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, B, Tn, d, Nst, hippo=hippo, limit=not hippo)
+    y, so = nat.selective_scan(T(u), T(dt), T(Bm), T(Cm), T(log_A), T(D), T(st))
+    ry, rs = O.ssm_scan(u, dt, Bm, Cm, log_A, D, st, "fp32")
+    np.testing.assert_allclose(N(y), ry, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(N(so), rs, rtol=1e-4, atol=1e-6)
+
+
+def test_selective_scan_general_input_and_T1(nat):
+    """Non-binary u (the layer accepts any input, tests/test_model.py:141) and T = 1."""
+    rng = np.random.default_rng(5)
+    u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, 2, 33, 40, 16)
+    u = rng.normal(0, 1, u.shape).astype(np.float32)
+    y, so = nat.selective_scan(T(u), T(dt), T(Bm), T(Cm), T(log_A), T(D), T(st))
+    ry, rs = O.ssm_scan(u, dt, Bm, Cm, log_A, D, st, "fp32")
+    np.testing.assert_allclose(N(y), ry, rtol=1e-4, atol=1e-5)
+    y1, s1 = nat.selective_scan(T(u[:, :1]), T(dt[:, :1]), T(Bm[:, :1]), T(Cm[:, :1]), T(log_A), T(D), T(st))
+    ry1, rs1 = O.ssm_scan(u[:, :1], dt[:, :1], Bm[:, :1], Cm[:, :1], log_A, D, st, "fp32")
+    np.testing.assert_allclose(N(y1), ry1, rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(N(s1), rs1, rtol=1e-4, atol=1e-7)
+
+
+def test_selective_scan_streaming_split(nat):
+    """Full sequence == two halves with carried state (the reference's continuity test)."""
+    rng = np.random.default_rng(6)
+    u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, 2, 120, 64, 32)
+    args = [T(a) for a in (u, dt, Bm, Cm)]
+    y, s = nat.selective_scan(*args, T(log_A), T(D), None)
+    y1, s1 = nat.selective_scan(*(a[:, :50] for a in args), T(log_A), T(D), None)
+    y2, s2 = nat.selective_scan(*(a[:, 50:] for a in args), T(log_A), T(D), s1)
+    np.testing.assert_allclose(N(torch.cat([y1, y2], 1)), N(y), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(N(s2), N(s), rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("hippo", [True, False])
+def test_selective_scan_bf16_gated(nat, hippo):
+    """bf16 activations, fp32 state.  A bf16 model's log_A = bf16(log(n+1)) is
+    recognised as HiPPO (within 2 bf16 ulps) and scanned with the exact
+    A = -(n+1); other A values are rounded to bf16 like the reference's op."""
+    rng = np.random.default_rng(8)
+    u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, 2, 64, 128, 32, hippo=hippo)
+    g = rng.normal(0, 1, u.shape).astype(np.float32)
+    dt, Bm, Cm, D, g = O.bf16(dt), O.bf16(Bm), O.bf16(Cm), O.bf16(D), O.bf16(g)
+    bf = torch.bfloat16
+    y, so = nat.selective_scan(T(u, bf), T(dt, bf), T(Bm, bf), T(Cm, bf), T(log_A, bf), T(D, bf), T(st),
+                               gate=T(g, bf), state_dtype=torch.float32)
+    if hippo:
+        ry, rs = O.ssm_scan(u, dt, Bm, Cm, log_A, D, st, "fp32")
+    else:
+        ry, rs = O.ssm_scan(u, dt, Bm, Cm, O.bf16(log_A), D, st, "fp32", a_mode="bf16")
+    ro = O.bf16(O.bf16(ry) * O.silu(g, "bf16"))
+    np.testing.assert_allclose(N(y), ro, rtol=1.6e-2, atol=1e-2)
+    np.testing.assert_allclose(N(so), rs, rtol=1e-3, atol=1e-5)
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+def test_ssm_forward_golden(nat, mode):
+    from neuratensor_b200 import SelectiveSSMLayer
+    d = load_golden(f"ssm_{mode}.npz")
+    p = golden_params(d)
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    layer = SelectiveSSMLayer(d_model=24, d_state=16)
+    layer.load_state_dict({k: torch.from_numpy(v) for k, v in p.items()})
+    layer = layer.to(DEV).to(dt)
+    with torch.no_grad():
+        y, st = layer(T(gget(d, "u"), dt), T(gget(d, "st0"), dt))
+    if mode == "fp32":
+        np.testing.assert_allclose(N(y), gget(d, "y"), rtol=1e-4, atol=1e-6)
+        np.testing.assert_allclose(N(st), gget(d, "st"), rtol=1e-4, atol=1e-6)
+    else:   # reference bf16 state vs fp32 recurrence inside the kernel
+        np.testing.assert_allclose(N(y), gget(d, "y"), rtol=2e-2, atol=2e-2)
+        np.testing.assert_allclose(N(st), gget(d, "st"), rtol=5e-2, atol=2e-2)
+
+
+# --------------------------------------------------------------------------- #
+#  LIF -> selective scan (standalone fused op)                                 #
+# --------------------------------------------------------------------------- #
+
+def test_fused_op_golden(nat):
+    d = load_golden("fused_op.npz")
+    y, spk, mem, st = nat.lif_ssm_fused(T(gget(d, "x"), torch.bfloat16), T(gget(d, "delta"), torch.bfloat16),
+                                        T(gget(d, "Bm"), torch.bfloat16), T(gget(d, "Cm"), torch.bfloat16),
+                                        T(d["log_A"]), T(d["D"]), T(d["beta"]), T(d["theta"]), T(d["mem0"]),
+                                        T(d["st0"]))
+    np.testing.assert_array_equal(N(spk), unbits(d["spikes_bits"], d["spikes_shape"]))
+    np.testing.assert_array_equal(N(mem), d["mem"])
+    np.testing.assert_allclose(N(y), O.bf16(d["y"]), rtol=8e-3, atol=1e-5)
+    np.testing.assert_allclose(N(st), d["st"], rtol=1e-4, atol=1e-6)
+
+
+def make_fused_inputs(B, L, D, Nst, seed=0):
+    """Standalone-op workload: x~N(0,1); dt=softplus(N(0,1)-2); A=-(n+1); B,C~N(0,1/N); beta~U(.8,.99)."""
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    bf = torch.bfloat16
+    x = torch.randn(B, L, D, generator=g, device=DEV).to(bf)
+    delta = torch.nn.functional.softplus(torch.randn(B, L, D, generator=g, device=DEV) - 2.0).to(bf)
+    Bm = (torch.randn(B, L, Nst, generator=g, device=DEV) / Nst ** 0.5).to(bf)
+    Cm = (torch.randn(B, L, Nst, generator=g, device=DEV) / Nst ** 0.5).to(bf)
+    log_A = torch.log(torch.arange(1, Nst + 1, device=DEV, dtype=torch.float32)).expand(D, Nst).contiguous()
+    Dskip = torch.ones(D, device=DEV)
+    beta = torch.rand(D, generator=g, device=DEV) * 0.19 + 0.80
+    th = torch.ones(D, device=DEV)
+    mem0 = torch.randn(B, D, generator=g, device=DEV) * 0.5
+    st0 = torch.randn(B, D, Nst, generator=g, device=DEV) * 0.1
+    return x, delta, Bm, Cm, log_A, Dskip, beta, th, mem0, st0
+
+
+def test_fused_op_vs_oracle_moderate(nat):
+    args = make_fused_inputs(2, 256, 96, 64, seed=1)
+    y, spk, mem, st = nat.lif_ssm_fused(*args)
+    a = [N(t) for t in args]
+    ry, rspk, rmem, rst = O.fused_lif_scan(*a)
+    np.testing.assert_array_equal(N(spk), rspk)
+    np.testing.assert_array_equal(N(mem), rmem)
+    np.testing.assert_allclose(N(y), O.bf16(ry), rtol=8e-3, atol=1e-5)
+    np.testing.assert_allclose(N(st), rst, rtol=1e-4, atol=1e-6)
+
+
+def test_fused_op_full_size_properties(nat):
+    """B=16, L=4096, d=2304, N=64: spot-check channels against the oracle, density in range,
+    streaming split equals the full call."""
+    B, L, D, Nst = 16, 4096, 2304, 64
+    args = make_fused_inputs(B, L, D, Nst, seed=2)
+    count = torch.zeros((), dtype=torch.int64, device=DEV)
+    y, spk, mem, st = nat.lif_ssm_fused(*args, spike_count=count)
+    torch.cuda.synchronize()
+    density = int(count.item()) / (B * L * D)
+    assert 0.05 < density < 0.3, density
+    assert int(spk.sum().item()) == int(count.item())
+    assert torch.isfinite(y.float()).all()
+    sel = np.array([0, 1, 511, 1151, 2303])
+    x, delta, Bm, Cm, log_A, Dskip, beta, th, mem0, st0 = args
+    for b in (0, 15):
+        ry, rspk, rmem, rst = O.fused_lif_scan(N(x[b:b + 1]), N(delta[b:b + 1]), N(Bm[b:b + 1]), N(Cm[b:b + 1]),
+                                               N(log_A), N(Dskip), N(beta), N(th), N(mem0[b:b + 1]),
+                                               N(st0[b:b + 1]), channels=sel)
+        np.testing.assert_array_equal(N(spk[b:b + 1, :, sel]), rspk)
+        np.testing.assert_array_equal(N(mem[b:b + 1, sel]), rmem)
+        np.testing.assert_allclose(N(y[b:b + 1, :, sel]), O.bf16(ry), rtol=8e-3, atol=1e-4)
+        np.testing.assert_allclose(N(st[b:b + 1, sel]), rst, rtol=1e-3, atol=1e-5)
+    # split at L/2 with carried membrane and state
+    h = L // 2
+    ya, _, ma, sa = nat.lif_ssm_fused(*(t[:, :h] for t in args[:4]), *args[4:8], mem0, st0)
+    yb, _, mb, sb = nat.lif_ssm_fused(*(t[:, h:] for t in args[:4]), *args[4:8], ma, sa)
+    assert torch.equal(torch.cat([ya, yb], 1), y)
+    assert torch.equal(mb, mem)
+    assert torch.equal(sb, st)
+
+
+# --------------------------------------------------------------------------- #
+#  (c) sparse out_proj                                                         #
+# --------------------------------------------------------------------------- #
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("case", ["p10", "p25", "p50", "p70", "exact50", "none"])
+def test_sparse_out_proj_golden(nat, mode, case):
+    d = load_golden(f"sparse_out_{mode}.npz")
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    o = T(gget(d, f"{case}_o"), dt)
+    s = T(unbits(d[f"{case}_spikes_bits"], d[f"{case}_spikes_shape"]), dt)
+    out, n_active = nat.sparse_out_proj(o, s, T(gget(d, "W"), dt))
+    ref = gget(d, f"{case}_out")
+    act = unbits(d[f"{case}_spikes_bits"], d[f"{case}_spikes_shape"]).any(-1)
+    assert int(n_active.item()) == int(act.sum())
+    if mode == "fp32":
+        np.testing.assert_allclose(N(out), ref, rtol=1e-4, atol=1e-5)
+    else:
+        np.testing.assert_allclose(N(out), ref, rtol=1.6e-2, atol=1e-2)
+    if 2 * act.sum() <= act.size:
+        assert np.all(N(out)[~act] == 0)
+
+
+@pytest.mark.parametrize("p", [0.1, 0.25, 0.5, 0.6])
+def test_sparse_out_proj_bf16_large(nat, p):
+    """M=4096 rows, K=1024, Nout=512 with Bernoulli(p) active rows (standalone-op layout)."""
+    g = torch.Generator(device=DEV).manual_seed(int(p * 100))
+    M, K, Nout = 4096, 1024, 512
+    act = torch.rand(M, generator=g, device=DEV) < p
+    s = ((torch.rand(M, K, generator=g, device=DEV) < 0.2) & act[:, None]).to(torch.bfloat16)
+    s[:, 0] = act.to(torch.bfloat16)
+    o = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
+    W = (torch.randn(Nout, K, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    out, n_active = nat.sparse_out_proj(o, s, W)
+    ref = O.sparse_out_proj(N(o)[None], N(s)[None], N(W), "bf16")[0]
+    assert int(n_active.item()) == int(act.sum().item())
+    np.testing.assert_allclose(N(out), ref, rtol=1.6e-2, atol=2e-3)
+
+
+# --------------------------------------------------------------------------- #
+#  (d) RMSNorm + in_proj                                                       #
+# --------------------------------------------------------------------------- #
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("M,dm,di", [(64, 96, 192), (333, 640, 1280), (1000, 200, 136)])
+def test_rmsnorm_in_proj_vs_oracle(nat, mode, M, dm, di):
+    rng = np.random.default_rng(M)
+    x = (rng.normal(0, 0.5, (M, dm))).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, dm).astype(np.float32)
+    W = (rng.normal(0, 1, (2 * di, dm)) / np.sqrt(dm)).astype(np.float32)
+    if mode == "bf16":
+        x, gamma, W = O.bf16(x), O.bf16(gamma), O.bf16(W)
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    h, gate = nat.rmsnorm_in_proj(T(x, dt), T(gamma, dt), T(W, dt))
+    xn = O.rmsnorm(x, gamma, mode)
+    ref = O._mm(xn, W, mode)
+    tol = dict(rtol=1e-4, atol=1e-5) if mode == "fp32" else dict(rtol=1.6e-2, atol=1e-2)
+    np.testing.assert_allclose(N(h), ref[:, :di], **tol)
+    np.testing.assert_allclose(N(gate), ref[:, di:], **tol)
+    if mode == "bf16":   # a GEMM summation-order difference moves at most one bf16 ulp, rarely
+        mism = (N(h) != ref[:, :di]).mean()
+        assert mism < 5e-3, mism
+
+
+# --------------------------------------------------------------------------- #
+#  FusedSpikeBlock                                                             #
+# --------------------------------------------------------------------------- #
+
+def _golden_block(d, dtype=torch.float32):
+    from neuratensor_b200 import FusedSpikeBlock
+    blk = FusedSpikeBlock(d_model=24, d_state=8, expand=2)
+    blk.load_state_dict({k: torch.from_numpy(v) for k, v in golden_params(d).items()})
+    return blk.to(DEV).to(dtype).eval()
+
+
+def test_block_forward_golden_fp32(nat):
+    d = load_golden("block_fp32.npz")
+    blk = _golden_block(d)
+    x = T(d["x"])
+    with torch.no_grad():
+        o1, s1, m1 = blk(x[:, :18])
+        o2, s2, m2 = blk(x[:, 18:], s1)
+    np.testing.assert_allclose(N(o1), d["out1"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(N(o2), d["out2"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(N(s1.membrane), d["mem1"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(N(s2.ssm_state), d["st2"], rtol=1e-4, atol=1e-6)
+    assert m1["spike_rate"] == pytest.approx(float(d["rate1"]), abs=2e-3)
+    assert m1["mean_beta"] == pytest.approx(float(d["mean_beta"]), rel=1e-6)
+
+
+@pytest.mark.parametrize("sparse_rows", [False, True])
+def test_block_forward_bf16_vs_oracle(nat, sparse_rows):
+    """bf16 block on one input: spikes and outputs against the oracle (dense and sparse branch)."""
+    from neuratensor_b200 import FusedSpikeBlock
+    torch.manual_seed(9)
+    blk = FusedSpikeBlock(d_model=64, d_state=16, expand=2)
+    with torch.no_grad():
+        blk.ssm.dt_proj.bias.normal_(-1.5, 0.5)
+        if sparse_rows:
+            blk.in_proj.weight.mul_(0.3)   # few active rows -> sparse out_proj branch
+    blk = blk.to(DEV).to(torch.bfloat16).eval()
+    p = O.params_from_state_dict(blk.state_dict())
+    rng = np.random.default_rng(10)
+    x = O.bf16(rng.normal(0, 1.0, (2, 150, 64)).astype(np.float32))
+    cap = {}
+    ro, rst, rm = O.block_forward(x, p, None, "bf16", capture=cap)
+    with torch.no_grad():
+        out, st, m = blk(T(x, torch.bfloat16))
+    if sparse_rows:
+        assert 2 * cap["spikes"].any(-1).sum() <= cap["spikes"].any(-1).size
+    agree = (N(out) == ro).mean()
+    np.testing.assert_allclose(N(out), ro, rtol=2e-2, atol=2e-2)
+    assert agree > 0.9, agree
+    assert m["spike_rate"] == pytest.approx(rm["spike_rate"], rel=2e-2)

@@ -126,7 +126,7 @@ BlockWs block_ws(void* ws, int dtype, int64_t M, int64_t dm, int64_t di, int64_t
     w.dt = c.take<char>(M * di * es);
     w.bc = c.take<char>(M * 2 * N * es);
     w.o = c.take<char>(M * di * es);
-    w.partials = c.take<unsigned short>(M * ((di + 127) / 128) * 2);
+    w.partials = c.take<unsigned short>(M * ((di + kLifChannels - 1) / kLifChannels) * 2);
     w.flags = c.take<unsigned char>(M);
     w.pos = c.take<int>(M * 4);
     w.idx = c.take<int>(M * 4);
@@ -340,7 +340,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         NT_TRY(launch_gemm(dtype, g, st));
     }
     // (a) LIF -> spikes, membrane, per-row counts
-    const int64_t n_cblk = (di + 127) / 128;
+    const int64_t n_cblk = (di + kLifChannels - 1) / kLifChannels;
     {
         LifArgs a{B, T, di, w.h, T * di, di, beta, threshold, mem_in, mem_out, w.spikes, T * di, di,
                   spike_count, w.partials, n_cblk};

@@ -53,6 +53,83 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& e, int64_t row, int64_t
     }
 }
 
+// Eight consecutive columns [col, col+8) of one row.  Vector path: the eight
+// outputs leave as one 16-byte store (bf16) when the host marked the output
+// layout 16-byte compatible (e.vec) and the group lies inside [0, N) on one
+// side of `split`; scalar fallback otherwise.
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&o)[8]) {
+    uint4 r;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 p = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&p);
+    }
+    return r;
+}
+__device__ __forceinline__ void unpack_bf16x8(uint4 q, float (&o)[8]) {
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        o[2 * i] = __uint_as_float(w[i] << 16);
+        o[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+template <int KIND>
+__device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, int64_t col, int64_t N,
+                                                const float (&acc)[8]) {
+    using E = Elem<NT_BF16>;
+    const bool full = e.vec && (col + 8 <= N);
+    if (!full) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (col + j < N) epi_apply<NT_BF16, KIND>(e, row, col + j, acc[j]);
+        return;
+    }
+    float o[8];
+    __nv_bfloat16* dst;
+    if (KIND == EPI_STORE) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = acc[j];
+        dst = static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col;
+    } else if (KIND == EPI_SPLIT2) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = acc[j];
+        dst = col < e.split ? static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col
+                            : static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
+    } else if (KIND == EPI_SSM_PROJ) {
+        if (col < e.split) {
+            float bias[8];
+            unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.bias) + col)), bias);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float v = E::rnd(acc[j] + bias[j]);
+                o[j] = v > 20.f ? v : log1pf(expf(v));
+            }
+            dst = static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = acc[j];
+            dst = static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
+        }
+    } else if (KIND == EPI_OUT_PROJ) {
+        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+        const float s = E::load(static_cast<const __nv_bfloat16*>(e.scale));
+        float res[8];
+        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.resid) + r * e.ldr + col)), res);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = E::rnd(E::rnd(E::rnd(acc[j]) * s) + res[j]);
+        dst = static_cast<__nv_bfloat16*>(e.out) + r * e.ldo + col;
+    } else {  // EPI_SCATTER
+        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = acc[j];
+        dst = static_cast<__nv_bfloat16*>(e.out) + r * e.ldo + col;
+    }
+    *reinterpret_cast<uint4*>(dst) = pack_bf16x8(o);
+}
+
 // ---------------------------------------------------------------------------
 // PTX wrappers (sm_100a)
 // ---------------------------------------------------------------------------
@@ -159,7 +236,7 @@ struct TcSmem {
 };
 
 template <int KIND, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                int64_t M, int64_t N, int64_t K, const int* m_count, EpiArgs epi, unsigned* err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -241,9 +318,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
                 if (row < m_eff) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int64_t col = n0 + c + j;
-                        if (col < N) epi_apply<NT_BF16, KIND>(epi, row, col, v[j]);
+                    for (int g = 0; g < 4; ++g) {
+                        const float (&v8)[8] = *reinterpret_cast<const float(*)[8]>(v + 8 * g);
+                        epi_apply8_bf16<KIND>(epi, row, n0 + c + 8 * g, N, v8);
                     }
                 }
             }
@@ -361,16 +438,28 @@ static int launch_tc(const GemmArgs& g, cudaStream_t stream) {
 
 template <int KIND>
 static int launch_kind(int dtype, const GemmArgs& g, cudaStream_t stream) {
-    if (dtype == NT_BF16) return launch_tc<KIND, 128, 4>(g, stream);
+    if (dtype == NT_BF16) return launch_tc<KIND, 128, 3>(g, stream);
     dim3 grid((unsigned)((g.N + 63) / 64), (unsigned)((g.M + 63) / 64));
     gemm_f32_kernel<KIND><<<grid, 256, 0, stream>>>(g.M, g.N, g.K, static_cast<const float*>(g.A), g.lda,
                                                      static_cast<const float*>(g.Bw), g.ldb, g.m_count, g.epi);
     return check_launch("gemm_f32_kernel");
 }
 
-int launch_gemm(int dtype, const GemmArgs& g, cudaStream_t stream) {
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int launch_gemm(int dtype, const GemmArgs& g_in, cudaStream_t stream) {
     if (dtype != NT_F32 && dtype != NT_BF16) return fail(NT_ERR_DTYPE, "gemm: dtype %d", dtype);
-    if (g.M <= 0 || g.N <= 0 || g.K <= 0) return NT_OK;
+    if (g_in.M <= 0 || g_in.N <= 0 || g_in.K <= 0) return NT_OK;
+    GemmArgs g = g_in;
+    {
+        // 16-byte epilogue stores need every 8-column group of every output row aligned
+        const EpiArgs& e = g.epi;
+        bool v = dtype == NT_BF16 && al16(e.out) && e.ldo % 8 == 0;
+        if (e.kind == EPI_SPLIT2 || e.kind == EPI_SSM_PROJ) v = v && e.split % 8 == 0 && al16(e.out2) && e.ldo2 % 8 == 0;
+        if (e.kind == EPI_SSM_PROJ) v = v && al16(e.bias);
+        if (e.kind == EPI_OUT_PROJ) v = v && al16(e.resid) && e.ldr % 8 == 0;
+        g.epi.vec = v ? 1 : 0;
+    }
     switch (g.epi.kind) {
         case EPI_STORE: return launch_kind<EPI_STORE>(dtype, g, stream);
         case EPI_SPLIT2: return launch_kind<EPI_SPLIT2>(dtype, g, stream);

@@ -4,6 +4,10 @@
 
 namespace nt {
 
+// Channels per LIF CTA; the block path's per-row partial counts have
+// ceil(C / kLifChannels) entries per row.
+constexpr int kLifChannels = 64;
+
 struct LifArgs {
     int64_t B, T, C;
     const void* x; int64_t x_sb, x_st;
@@ -12,7 +16,7 @@ struct LifArgs {
     void* spikes; int64_t s_sb, s_st;
     unsigned long long* spike_count;       // optional, += spikes
     unsigned short* row_partials;          // optional [B*T][n_cblk] per-row counts
-    int64_t n_cblk;                        // = ceil(C/128)
+    int64_t n_cblk;                        // = ceil(C / kLifChannels)
 };
 // math: NT_F32 (exact fp32 recurrence) or NT_BF16 (bf16 rounding after each op)
 int launch_lif_scan(int dtype, int math, const LifArgs& a, cudaStream_t stream);
@@ -84,6 +88,7 @@ struct EpiArgs {
     const void* scale;         // EPI_OUT_PROJ: pointer to one dtype value
     const void* resid; int64_t ldr;
     const int* row_idx;        // row map for compacted A rows (nullptr: identity)
+    int vec;                   // 1: outputs, residual and bias allow 16-byte accesses per 8 columns
 };
 struct GemmArgs {
     int64_t M, N, K;

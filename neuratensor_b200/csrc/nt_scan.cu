@@ -89,14 +89,14 @@ struct ScanSmem {
     static constexpr int NP = kNpt * TPC;
     static constexpr int RAW = 3 * kTch * CPB + 2 * kTch * NP;       // elements of T per staging buffer
     static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
-    static constexpr int WORK_FLOATS = 2 * kTch * CPB + 2 * kTch * NP + kTch * 128 + kTch * CPB;
+    static constexpr int WORK_FLOATS = 2 * kTch * CPB + 2 * kTch * NP + kTch * 128 + kTch * CPB + CPB + kTch;
     static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + sizeof(float) * (size_t)WORK_FLOATS;
 };
 
 // MODE 0: selective scan with given u.  MODE 1: u = LIF spikes of x (fused op).
 template <int DT, int SDT, int TPC, int MODE>
 __global__ void __launch_bounds__(128)
-scan_kernel(ScanArgs a, FusedArgs f) {
+ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
     using L = ScanSmem<TPC, T>;
     constexpr int CPB = L::CPB, NP = L::NP;
@@ -107,6 +107,8 @@ scan_kernel(ScanArgs a, FusedArgs f) {
     float* w_C = w_B + kTch * NP;                                        // [kTch][NP]
     float* w_yp = w_C + kTch * NP;                                       // [kTch][128] partial C.h
     float* w_s = w_yp + kTch * 128;                                      // [kTch][CPB] spikes (MODE 1)
+    float* w_D = w_s + kTch * CPB;                                       // [CPB] skip weights D
+    int* w_pos = reinterpret_cast<int*>(w_D + CPB);                      // [kTch] compacted row positions
 
     const int64_t T_len = MODE ? f.L : a.T, d = MODE ? f.d : a.d, N = MODE ? f.N : a.N;
     const T* p_u = static_cast<const T*>(MODE ? f.x : a.u);
@@ -170,6 +172,11 @@ scan_kernel(ScanArgs a, FusedArgs f) {
         th = f.threshold[c];
         if (f.mem_in) mem = f.mem_in[b * d + c];
     }
+    for (int i = tid; i < CPB; i += 128) {
+        const int64_t cg = c0 + i;
+        w_D[i] = cg < d ? (MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + cg) : f.Dskip[cg])
+                        : 0.f;
+    }
     unsigned spike_local = 0;
     const bool sparse_rows = (MODE == 0) && a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
 
@@ -218,6 +225,7 @@ scan_kernel(ScanArgs a, FusedArgs f) {
             w_B[i] = to_f(rb[3 * kTch * CPB + i]);
             w_C[i] = to_f(rb[3 * kTch * CPB + kTch * NP + i]);
         }
+        if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
         __syncthreads();
         // ---- recurrence ------------------------------------------------------
         const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
@@ -295,15 +303,14 @@ scan_kernel(ScanArgs a, FusedArgs f) {
 #pragma unroll
             for (int s2 = 0; s2 < TPC; ++s2) yp += w_yp[tt * 128 + cc * TPC + s2];
             const float uu = MODE == 0 ? w_u[i] : w_s[i];
-            const float Dc = MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + cg) : f.Dskip[cg];
-            const float yv = __fadd_rn(yp, __fmul_rn(Dc, uu));
+            const float yv = __fadd_rn(yp, __fmul_rn(w_D[cc], uu));
             int64_t row = row0 + t;
             if (MODE == 0) {
                 using E = Elem<DT>;
                 float o = E::rnd(yv);
                 if (has_gate) o = E::rnd(o * E::rnd(silu_f(to_f(rb[2 * kTch * CPB + i]))));
                 if (sparse_rows) {
-                    const int pos = a.row_pos[row];
+                    const int pos = w_pos[tt];
                     if (pos < 0) continue;
                     row = pos;
                 }
@@ -350,14 +357,14 @@ template <int DT, int SDT, int MODE, int TPC>
 int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
     const size_t smem = ScanSmem<TPC, T>::BYTES;
-    auto kern = scan_kernel<DT, SDT, TPC, MODE>;
+    auto kern = ssm_scan_kernel<DT, SDT, TPC, MODE>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
     const int64_t d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
     constexpr int CPB = 128 / TPC;
     dim3 grid((unsigned)((d + CPB - 1) / CPB), (unsigned)B);
     kern<<<grid, 128, smem, stream>>>(a, f);
-    return check_launch("scan_kernel");
+    return check_launch("ssm_scan_kernel");
 }
 
 template <int DT, int SDT, int MODE>

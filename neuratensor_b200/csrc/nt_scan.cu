@@ -26,9 +26,10 @@
 // channel of the CTA (the reference's initialisation, ssm.py:34-43), a
 // thread needs two exponentials per step and a chain of multiplies:
 // exp(dt*A[c,n+1]) = exp(dt*A[c,n]) * exp(dt*A[c,0]).  The structure test is
-// 1e-6 relative for float32 parameters and 2 bf16 ulps for bfloat16 ones
-// (a bf16 model stores log(n+1) rounded, so exp(log_A) lands within an ulp or
-// two of n+1); on the fast path A is exactly (n+1)*A[c,0].
+// 1e-6 relative on A for float32 parameters; for bfloat16 parameters it is
+// made on log_A (one bf16 ulp of log(n+1) + log_A[c,0]), because a bf16 model
+// stores log(n+1) rounded and exp() of that lands up to ~2% away from n+1.
+// On the fast path A is exactly (n+1)*A[c,0].
 #include "nt_kernels.cuh"
 
 #include <type_traits>
@@ -130,11 +131,19 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             return -Elem<DT>::rnd(expf(Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.log_A) + c * N + n)));
         return -expf(f.log_A[c * N + n]);
     };
-    const float tol = (MODE == 0 && DT == NT_BF16) ? 7.8125e-3f : 1e-6f;
+    // HiPPO structure test.  fp32 parameters: A[c,n] == (n+1)*A[c,0] to 1e-6
+    // relative.  bf16 parameters: log_A[c,n] == log(n+1) + log_A[c,0] to one
+    // bf16 ulp of the stored value, i.e. the parameter is the HiPPO init up to
+    // its own storage rounding.
+    constexpr bool kBf16Params = (MODE == 0 && DT == NT_BF16);
+    auto load_logA = [&](int64_t n) -> float {
+        return Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.log_A) + c * N + n);
+    };
     float A2[kNpt], cinv[kNpt], h[kNpt];
     unsigned lim_mask = 0;
     bool hippo_ok = true;
     const float Abase = live ? load_A(0) : -1.f;
+    const float la0 = (live && kBf16Params) ? load_logA(0) : 0.f;
     const void* sin = MODE ? (const void*)f.state_in : a.state_in;
 #pragma unroll
     for (int j = 0; j < kNpt; ++j) {
@@ -148,12 +157,20 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                 if (MODE == 0 && SDT == NT_BF16) h[j] = __bfloat162float(static_cast<const __nv_bfloat16*>(sin)[si]);
                 else h[j] = static_cast<const float*>(sin)[si];
             }
-            if (fabsf(A - (float)(n + 1) * Abase) > tol * fabsf(A)) hippo_ok = false;
+            if (kBf16Params) {
+                const float la = load_logA(n);
+                int e2;
+                frexpf(la, &e2);                                   // |la| in [2^(e2-1), 2^e2)
+                const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
+                if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) hippo_ok = false;
+            } else if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) {
+                hippo_ok = false;
+            }
         }
         const bool lim = (live && n < N) && fabsf(A) < 1e-6f;
         if (lim) { lim_mask |= 1u << j; hippo_ok = false; }
         A2[j] = A * kLog2e;
-        cinv[j] = (A == 0.f) ? 0.f : 1.0f / A;
+        cinv[j] = (lim || A == 0.f) ? 0.f : 1.0f / A;   // limit states take B_bar = dt*B
     }
     const bool hippo = __syncthreads_and(hippo_ok ? 1 : 0) != 0;
     if (hippo) {
@@ -166,6 +183,14 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         }
     }
     const float q2 = Abase * kLog2e;
+    // packed per-state constants: 1/A, -1/A and the |A| < 1e-6 selector
+    float2 ci2[kNpt / 2], nci2[kNpt / 2], lim2[kNpt / 2];
+#pragma unroll
+    for (int j = 0; j < kNpt / 2; ++j) {
+        ci2[j] = make_float2(cinv[2 * j], cinv[2 * j + 1]);
+        nci2[j] = make_float2(-cinv[2 * j], -cinv[2 * j + 1]);
+        lim2[j] = make_float2((lim_mask >> (2 * j)) & 1u ? 1.f : 0.f, (lim_mask >> (2 * j + 1)) & 1u ? 1.f : 0.f);
+    }
     float beta = 0.f, th = 0.f, mem = 0.f;
     if (live && MODE == 1) {
         beta = f.beta[c];
@@ -263,14 +288,16 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                                   make_float2(k1.z, k1.w)};
             float2 hv[4] = {make_float2(h[0], h[1]), make_float2(h[2], h[3]), make_float2(h[4], h[5]),
                             make_float2(h[6], h[7])};
-            if (u != 0.f) {
+            // Input term only when some lane of the warp has u != 0 (warp-uniform
+            // branch, no divergence); for u == 0 it adds exactly zero.
+            if (__any_sync(0xffffffffu, u != 0.f)) {
                 const float2 uu = make_float2(u, u);
 #pragma unroll
                 for (int j = 0; j < kNpt / 2; ++j) {
-                    float2 coef;
-                    coef.x = ((lim_mask >> (2 * j)) & 1u) ? dtv : (av[j].x - 1.0f) * cinv[2 * j];
-                    coef.y = ((lim_mask >> (2 * j + 1)) & 1u) ? dtv : (av[j].y - 1.0f) * cinv[2 * j + 1];
-                    const float2 bu = __fmul2_rn(__fmul2_rn(coef, Bv[j]), uu);
+                    // (A_bar - 1)/A as one fma; states with |A| < 1e-6 use dt instead
+                    float2 coef = __ffma2_rn(av[j], ci2[j], nci2[j]);
+                    if (!HIP) coef = __ffma2_rn(make_float2(dtv, dtv), lim2[j], coef);
+                    const float2 bu = __fmul2_rn(coef, __fmul2_rn(Bv[j], uu));
                     hv[j] = __ffma2_rn(av[j], hv[j], bu);
                 }
             } else {

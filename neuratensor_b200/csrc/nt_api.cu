@@ -202,7 +202,7 @@ int nt_selective_scan(int dtype, int state_dtype, int64_t B, int64_t T, int64_t 
     if (B > 65535) return fail(NT_ERR_ARG, "nt_selective_scan: B > 65535");
     if (!u || !dt || !Bm || !Cm || !log_A || !D || !state_out || !y)
         return fail(NT_ERR_ARG, "nt_selective_scan: null pointer");
-    ScanArgs a{B, T, d, N, u, dt, Bm, Cm, N, log_A, D, gate, state_in, state_out, y, nullptr, nullptr};
+    ScanArgs a{B, T, d, N, u, dt, Bm, Cm, N, log_A, D, gate, state_in, state_out, y, nullptr, nullptr, 0};
     return launch_selective_scan(dtype, state_dtype, a, as_stream(stream));
 }
 
@@ -232,7 +232,7 @@ int nt_ssm_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d, 
     NT_TRY(launch_gemm(dtype, g, st));
     const char* bc = static_cast<const char*>(w.bc);
     ScanArgs a{B, T, d, N, u, w.dt, bc, bc + N * esize(dtype), 2 * N, log_A, D, nullptr, state_in, state_out, y,
-               nullptr, nullptr};
+               nullptr, nullptr, 0};
     return launch_selective_scan(dtype, state_dtype, a, st);
 }
 
@@ -336,7 +336,8 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         GemmArgs g{};
         g.M = M; g.N = 2 * di; g.K = dm;
         g.A = w.xn; g.lda = dm; g.Bw = W_in; g.ldb = dm;
-        g.epi.kind = EPI_SPLIT2; g.epi.out = w.h; g.epi.ldo = di; g.epi.out2 = w.gate; g.epi.ldo2 = di; g.epi.split = di;
+        g.epi.kind = EPI_SPLIT2_SILU; g.epi.out = w.h; g.epi.ldo = di; g.epi.out2 = w.gate; g.epi.ldo2 = di;
+        g.epi.split = di;
         NT_TRY(launch_gemm(dtype, g, st));
     }
     // (a) LIF -> spikes, membrane, per-row counts
@@ -362,7 +363,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
     {
         const char* bc = static_cast<const char*>(w.bc);
         ScanArgs a{B, T, di, N, w.spikes, w.dt, bc, bc + N * es, 2 * N, log_A, D, w.gate, state_in, state_out, w.o,
-                   w.pos, w.counters + 1};
+                   w.pos, w.counters + 1, /*gate_is_silu=*/1};
         NT_TRY(launch_selective_scan(dtype, state_dtype, a, st));
     }
     // (c) out_proj on the processed rows, * out_scale + residual, scattered back

@@ -30,6 +30,14 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& e, int64_t row, int64_t
     } else if (KIND == EPI_SPLIT2) {
         if (col < e.split) static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(acc);
         else static_cast<T*>(e.out2)[row * e.ldo2 + (col - e.split)] = E::from_f(acc);
+    } else if (KIND == EPI_SPLIT2_SILU) {
+        // h as computed; gate -> rnd(silu(rnd(gate))) as the reference's F.silu (fused.py:130)
+        if (col < e.split) {
+            static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(acc);
+        } else {
+            const float g = E::rnd(acc);
+            static_cast<T*>(e.out2)[row * e.ldo2 + (col - e.split)] = E::from_f(g / (1.0f + expf(-g)));
+        }
     } else if (KIND == EPI_SSM_PROJ) {
         if (col < e.split) {
             // dt = softplus(u W_dt^T + b_dt)  (ssm.py:330; threshold 20)
@@ -98,6 +106,19 @@ __device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, i
         for (int j = 0; j < 8; ++j) o[j] = acc[j];
         dst = col < e.split ? static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col
                             : static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
+    } else if (KIND == EPI_SPLIT2_SILU) {
+        if (col < e.split) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = acc[j];
+            dst = static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float g = E::rnd(acc[j]);
+                o[j] = g / (1.0f + expf(-g));
+            }
+            dst = static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
+        }
     } else if (KIND == EPI_SSM_PROJ) {
         if (col < e.split) {
             float bias[8];
@@ -455,7 +476,8 @@ int launch_gemm(int dtype, const GemmArgs& g_in, cudaStream_t stream) {
         // 16-byte epilogue stores need every 8-column group of every output row aligned
         const EpiArgs& e = g.epi;
         bool v = dtype == NT_BF16 && al16(e.out) && e.ldo % 8 == 0;
-        if (e.kind == EPI_SPLIT2 || e.kind == EPI_SSM_PROJ) v = v && e.split % 8 == 0 && al16(e.out2) && e.ldo2 % 8 == 0;
+        if (e.kind == EPI_SPLIT2 || e.kind == EPI_SSM_PROJ || e.kind == EPI_SPLIT2_SILU)
+            v = v && e.split % 8 == 0 && al16(e.out2) && e.ldo2 % 8 == 0;
         if (e.kind == EPI_SSM_PROJ) v = v && al16(e.bias);
         if (e.kind == EPI_OUT_PROJ) v = v && al16(e.resid) && e.ldr % 8 == 0;
         g.epi.vec = v ? 1 : 0;
@@ -466,6 +488,7 @@ int launch_gemm(int dtype, const GemmArgs& g_in, cudaStream_t stream) {
         case EPI_SSM_PROJ: return launch_kind<EPI_SSM_PROJ>(dtype, g, stream);
         case EPI_OUT_PROJ: return launch_kind<EPI_OUT_PROJ>(dtype, g, stream);
         case EPI_SCATTER: return launch_kind<EPI_SCATTER>(dtype, g, stream);
+        case EPI_SPLIT2_SILU: return launch_kind<EPI_SPLIT2_SILU>(dtype, g, stream);
         default: return fail(NT_ERR_ARG, "gemm: epilogue kind %d", g.epi.kind);
     }
 }

@@ -32,6 +32,7 @@ struct ScanArgs {
     // says the sparse branch is taken, output row r goes to row row_pos[r]
     // (inactive rows are skipped).
     const int* row_pos; const int* sparse_flag;
+    int gate_is_silu;                       // gate already holds rnd(silu(gate))
 };
 int launch_selective_scan(int dtype, int state_dtype, const ScanArgs& a, cudaStream_t stream);
 
@@ -77,7 +78,8 @@ enum EpiKind : int {
     EPI_SPLIT2 = 1,       // cols [0,split) -> out, [split,N) -> out2 (in_proj h | gate)
     EPI_SSM_PROJ = 2,     // cols [0,split): softplus(acc + bias) -> out (dt); rest -> out2 (B|C)
     EPI_OUT_PROJ = 3,     // out[row_map(r)] = rnd(rnd(rnd(acc)*scale) + resid[row_map(r)])
-    EPI_SCATTER = 4       // out[row_map(r)] = acc  (sparse out_proj without scale)
+    EPI_SCATTER = 4,      // out[row_map(r)] = acc  (sparse out_proj without scale)
+    EPI_SPLIT2_SILU = 5   // cols [0,split) -> out (h), [split,N) -> out2 as rnd(silu(acc))
 };
 struct EpiArgs {
     int kind;

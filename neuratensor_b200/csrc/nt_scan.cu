@@ -288,21 +288,16 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                                   make_float2(k1.z, k1.w)};
             float2 hv[4] = {make_float2(h[0], h[1]), make_float2(h[2], h[3]), make_float2(h[4], h[5]),
                             make_float2(h[6], h[7])};
-            // Input term only when some lane of the warp has u != 0 (warp-uniform
-            // branch, no divergence); for u == 0 it adds exactly zero.
-            if (__any_sync(0xffffffffu, u != 0.f)) {
-                const float2 uu = make_float2(u, u);
+            // Branch-free input term (it is exactly zero when u == 0), so the
+            // unrolled steps stay one basic block the compiler can interleave.
+            const float2 uu = make_float2(u, u);
 #pragma unroll
-                for (int j = 0; j < kNpt / 2; ++j) {
-                    // (A_bar - 1)/A as one fma; states with |A| < 1e-6 use dt instead
-                    float2 coef = __ffma2_rn(av[j], ci2[j], nci2[j]);
-                    if (!HIP) coef = __ffma2_rn(make_float2(dtv, dtv), lim2[j], coef);
-                    const float2 bu = __fmul2_rn(coef, __fmul2_rn(Bv[j], uu));
-                    hv[j] = __ffma2_rn(av[j], hv[j], bu);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kNpt / 2; ++j) hv[j] = __fmul2_rn(av[j], hv[j]);
+            for (int j = 0; j < kNpt / 2; ++j) {
+                // (A_bar - 1)/A as one fma; states with |A| < 1e-6 use dt instead
+                float2 coef = __ffma2_rn(av[j], ci2[j], nci2[j]);
+                if (!HIP) coef = __ffma2_rn(make_float2(dtv, dtv), lim2[j], coef);
+                const float2 bu = __fmul2_rn(coef, __fmul2_rn(Bv[j], uu));
+                hv[j] = __ffma2_rn(av[j], hv[j], bu);
             }
 #pragma unroll
             for (int j = 0; j < kNpt / 2; ++j) { h[2 * j] = hv[j].x; h[2 * j + 1] = hv[j].y; }
@@ -335,7 +330,10 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             if (MODE == 0) {
                 using E = Elem<DT>;
                 float o = E::rnd(yv);
-                if (has_gate) o = E::rnd(o * E::rnd(silu_f(to_f(rb[2 * kTch * CPB + i]))));
+                if (has_gate) {
+                    const float g = to_f(rb[2 * kTch * CPB + i]);
+                    o = E::rnd(o * (a.gate_is_silu ? g : E::rnd(silu_f(g))));
+                }
                 if (sparse_rows) {
                     const int pos = w_pos[tt];
                     if (pos < 0) continue;

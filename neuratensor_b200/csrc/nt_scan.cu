@@ -3,10 +3,9 @@
 // standalone LIF -> selective-scan fusion.
 //
 // Work split: a channel's d_state recurrences are spread over TPC threads
-// (8 states each, TPC = next power of two >= N/8); each thread serves
-// kCpt = 2 channels, so the per-step B/C loads are shared by two channels and
-// the thread has two independent recurrences to interleave.  A 128-thread
-// CTA owns CPB = 2*128/TPC channels of one batch row and walks time serially.
+// (NPT = 8 states each, or 4 when the batch is too small to fill the GPU;
+// TPC = next power of two >= N/NPT).  A 128-thread CTA owns CPB = 128/TPC
+// channels of one batch row and walks time serially.
 //
 // Per chunk of TCH steps:
 //   1. cp.async stages the next chunk's raw inputs (u or x, dt, gate, B, C)
@@ -40,8 +39,6 @@ namespace nt {
 
 namespace {
 
-constexpr int kNpt = 8;     // d_state entries per thread
-constexpr int kCpt = 2;     // channels per thread (B/C loads shared between them)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
@@ -86,35 +83,33 @@ __device__ __forceinline__ void stage_tile(T* dst, const T* src, int64_t ld, int
     }
 }
 
-template <int TPC, typename T>
+template <int TPC, int NPT, typename T>
 struct ScanSmem {
     // time steps per staged chunk (halved where the channel or state tile is widest)
     static constexpr int TCH = (TPC == 1 || TPC == 32) ? 16 : 32;
-    static constexpr int G = 128 / TPC;                 // channel groups per CTA
-    static constexpr int CPB = G * kCpt;                // channels per CTA
-    static constexpr int NP = kNpt * TPC;               // padded d_state
+    static constexpr int CPB = 128 / TPC;               // channels per CTA
+    static constexpr int NP = NPT * TPC;                // padded d_state
     static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;       // elements of T per staging buffer
     static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
-    static constexpr int WORK_FLOATS = 2 * TCH * CPB + 2 * TCH * NP + TCH * 128 * kCpt + TCH * CPB + CPB + TCH;
+    static constexpr int WORK_FLOATS = 2 * TCH * CPB + 2 * TCH * NP + TCH * 128 + TCH * CPB + CPB + TCH;
     static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + sizeof(float) * (size_t)WORK_FLOATS;
 };
 
 // MODE 0: selective scan with given u.  MODE 1: u = LIF spikes of x (fused op).
-// Thread (g, sub) owns states [8*sub, 8*sub+8) of the kCpt channels
-// c0 + g + k*G, k < kCpt: B and C of a step are loaded once for kCpt channels.
-template <int DT, int SDT, int TPC, int MODE>
+// Thread (cl, sub) owns states [NPT*sub, NPT*sub + NPT) of channel c0 + cl.
+template <int DT, int SDT, int TPC, int NPT, int MODE>
 __global__ void __launch_bounds__(128)
 ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    using L = ScanSmem<TPC, T>;
-    constexpr int G = L::G, CPB = L::CPB, NP = L::NP, kTch = L::TCH;
+    using L = ScanSmem<TPC, NPT, T>;
+    constexpr int CPB = L::CPB, NP = L::NP, kTch = L::TCH, NPR = NPT / 2;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float* w_u = reinterpret_cast<float*>(smem_raw + 2 * L::RAW_BYTES);  // [kTch][CPB] u (or x)
     float* w_dt = w_u + kTch * CPB;                                      // [kTch][CPB]
     float* w_B = w_dt + kTch * CPB;                                      // [kTch][NP]  B (or B/(n+1))
     float* w_C = w_B + kTch * NP;                                        // [kTch][NP]
-    float* w_yp = w_C + kTch * NP;                                       // [kTch][kCpt][128] partial C.h
-    float* w_s = w_yp + kTch * 128 * kCpt;                               // [kTch][CPB] spikes (MODE 1)
+    float* w_yp = w_C + kTch * NP;                                       // [kTch][128] partial C.h
+    float* w_s = w_yp + kTch * 128;                                      // [kTch][CPB] spikes (MODE 1)
     float* w_D = w_s + kTch * CPB;                                       // [CPB] skip weights D
     int* w_pos = reinterpret_cast<int*>(w_D + CPB);                      // [kTch] compacted row positions
 
@@ -127,16 +122,13 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     const bool has_gate = p_g != nullptr;
     const int64_t ld_bc = (MODE == 0 && a.ld_bc > 0) ? a.ld_bc : N;
 
-    const int tid = threadIdx.x, g = tid / TPC, sub = tid % TPC;
-    const int64_t c0 = (int64_t)blockIdx.x * CPB, b = blockIdx.y;
-    int64_t ch[kCpt];
-    bool live[kCpt];
-#pragma unroll
-    for (int k = 0; k < kCpt; ++k) { ch[k] = c0 + g + k * G; live[k] = ch[k] < d; }
+    const int tid = threadIdx.x, cl = tid / TPC, sub = tid % TPC;
+    const int64_t c0 = (int64_t)blockIdx.x * CPB, c = c0 + cl, b = blockIdx.y;
+    const bool live = c < d;
 
     // ---- per-state constants -------------------------------------------------
     // A = -exp(log_A), rounded like the reference's own tensor op (ssm.py:121)
-    auto load_logA = [&](int64_t c, int64_t n) -> float {
+    auto load_logA = [&](int64_t n) -> float {
         if (MODE == 0) return Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.log_A) + c * N + n);
         return f.log_A[c * N + n];
     };
@@ -146,63 +138,57 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     // bf16 ulp of the stored value, i.e. the parameter is the HiPPO init up to
     // its own storage rounding.
     constexpr bool kBf16Params = (MODE == 0 && DT == NT_BF16);
-    float A2[kCpt][kNpt], cinv[kCpt][kNpt], h[kCpt][kNpt];
-    float Abase[kCpt];
-    unsigned lim_mask[kCpt];
+    float A2[NPT], cinv[NPT], h[NPT];
+    unsigned lim_mask = 0;
     bool hippo_ok = true;
+    const float la0 = live ? load_logA(0) : 0.f;
+    const float Abase = live ? A_of(la0) : -1.f;
     const void* sin = MODE ? (const void*)f.state_in : a.state_in;
 #pragma unroll
-    for (int k = 0; k < kCpt; ++k) {
-        lim_mask[k] = 0;
-        const float la0 = live[k] ? load_logA(ch[k], 0) : 0.f;
-        Abase[k] = live[k] ? A_of(la0) : -1.f;
-#pragma unroll
-        for (int j = 0; j < kNpt; ++j) {
-            const int64_t n = (int64_t)sub * kNpt + j;
-            float A = 0.f;
-            h[k][j] = 0.f;
-            const bool on = live[k] && n < N;
-            if (on) {
-                const float la = load_logA(ch[k], n);
-                A = A_of(la);
-                if (sin) {
-                    const int64_t si = (b * d + ch[k]) * N + n;
-                    if (MODE == 0 && SDT == NT_BF16) h[k][j] = __bfloat162float(static_cast<const __nv_bfloat16*>(sin)[si]);
-                    else h[k][j] = static_cast<const float*>(sin)[si];
-                }
-                if (kBf16Params) {
-                    int e2;
-                    frexpf(la, &e2);                                   // |la| in [2^(e2-1), 2^e2)
-                    const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
-                    if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) hippo_ok = false;
-                } else if (fabsf(A - (float)(n + 1) * Abase[k]) > 1e-6f * fabsf(A)) {
-                    hippo_ok = false;
-                }
+    for (int j = 0; j < NPT; ++j) {
+        const int64_t n = (int64_t)sub * NPT + j;
+        float A = 0.f;
+        h[j] = 0.f;
+        const bool on = live && n < N;
+        if (on) {
+            const float la = load_logA(n);
+            A = A_of(la);
+            if (sin) {
+                const int64_t si = (b * d + c) * N + n;
+                if (MODE == 0 && SDT == NT_BF16) h[j] = __bfloat162float(static_cast<const __nv_bfloat16*>(sin)[si]);
+                else h[j] = static_cast<const float*>(sin)[si];
             }
-            const bool lim = on && fabsf(A) < 1e-6f;
-            if (lim) { lim_mask[k] |= 1u << j; hippo_ok = false; }
-            A2[k][j] = A * kLog2e;
-            cinv[k][j] = (lim || A == 0.f) ? 0.f : 1.0f / A;   // limit states take B_bar = dt*B
+            if (kBf16Params) {
+                int e2;
+                frexpf(la, &e2);                                   // |la| in [2^(e2-1), 2^e2)
+                const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
+                if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) hippo_ok = false;
+            } else if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) {
+                hippo_ok = false;
+            }
         }
+        const bool lim = on && fabsf(A) < 1e-6f;
+        if (lim) { lim_mask |= 1u << j; hippo_ok = false; }
+        A2[j] = A * kLog2e;
+        cinv[j] = (lim || A == 0.f) ? 0.f : 1.0f / A;   // limit states take B_bar = dt*B
     }
     const bool hippo = __syncthreads_and(hippo_ok ? 1 : 0) != 0;
-    // HiPPO constants per channel: first-state exponent, ratio exponent, 1/A[c,0]
-    float a2first[kCpt], q2[kCpt], rA0[kCpt];
+    // HiPPO constants: first-state exponent, ratio exponent, 1/A[c,0]
+    const float a2first = (float)(sub * NPT + 1) * Abase * kLog2e;
+    const float q2 = Abase * kLog2e;
+    const float rA0 = 1.0f / Abase;
+    float2 ci2[NPR], nci2[NPR], lim2[NPR];
 #pragma unroll
-    for (int k = 0; k < kCpt; ++k) {
-        a2first[k] = (float)(sub * kNpt + 1) * Abase[k] * kLog2e;
-        q2[k] = Abase[k] * kLog2e;
-        rA0[k] = 1.0f / Abase[k];
+    for (int j = 0; j < NPR; ++j) {
+        ci2[j] = make_float2(cinv[2 * j], cinv[2 * j + 1]);
+        nci2[j] = make_float2(-cinv[2 * j], -cinv[2 * j + 1]);
+        lim2[j] = make_float2((lim_mask >> (2 * j)) & 1u ? 1.f : 0.f, (lim_mask >> (2 * j + 1)) & 1u ? 1.f : 0.f);
     }
-    float beta[kCpt], th[kCpt], mem[kCpt];
-#pragma unroll
-    for (int k = 0; k < kCpt; ++k) {
-        beta[k] = th[k] = mem[k] = 0.f;
-        if (MODE == 1 && live[k]) {
-            beta[k] = f.beta[ch[k]];
-            th[k] = f.threshold[ch[k]];
-            if (f.mem_in) mem[k] = f.mem_in[b * d + ch[k]];
-        }
+    float beta = 0.f, th = 0.f, mem = 0.f;
+    if (MODE == 1 && live) {
+        beta = f.beta[c];
+        th = f.threshold[c];
+        if (f.mem_in) mem = f.mem_in[b * d + c];
     }
     for (int i = tid; i < CPB; i += 128) {
         const int64_t cg = c0 + i;
@@ -236,6 +222,77 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         cp_async_commit();
     };
 
+    // one step; steps past the end of the sequence see u = dt = B = 0, which
+    // leaves the state unchanged (A_bar = 1, no input term)
+    auto step = [&](int tt, int nt, auto hip) {
+        constexpr bool HIP = decltype(hip)::value;
+        float Bf[NPT], Cf[NPT];
+#pragma unroll
+        for (int q = 0; q < NPT / 4; ++q) {
+            const float4 bq = reinterpret_cast<const float4*>(w_B + tt * NP + sub * NPT)[q];
+            const float4 cq = reinterpret_cast<const float4*>(w_C + tt * NP + sub * NPT)[q];
+            Bf[4 * q] = bq.x; Bf[4 * q + 1] = bq.y; Bf[4 * q + 2] = bq.z; Bf[4 * q + 3] = bq.w;
+            Cf[4 * q] = cq.x; Cf[4 * q + 1] = cq.y; Cf[4 * q + 2] = cq.z; Cf[4 * q + 3] = cq.w;
+        }
+        float u;
+        if (MODE == 0) {
+            u = w_u[tt * CPB + cl];
+        } else {
+            // LIF step (snn.py:177-181) in fp32, identical in every thread of the channel
+            const float m1 = __fadd_rn(__fmul_rn(beta, mem), w_u[tt * CPB + cl]);
+            const float s1 = (m1 >= th) ? 1.f : 0.f;
+            const float m2 = __fsub_rn(m1, __fmul_rn(th, s1));
+            const bool in_seq = tt < nt;
+            u = in_seq ? s1 : 0.f;
+            mem = in_seq ? m2 : mem;
+        }
+        const float dtv = w_dt[tt * CPB + cl];
+        float2 av[NPR], hv[NPR];
+#pragma unroll
+        for (int j = 0; j < NPR; ++j) hv[j] = make_float2(h[2 * j], h[2 * j + 1]);
+        if (HIP) {
+            // A[n] = (n+1) A0: exp(dt A[n]) by a chain of multiplies; the input term
+            // uses w = u/A0 * B/(n+1):  h' = A_bar (h + w) - w
+            const float a0 = ex2(dtv * a2first);
+            const float qv = ex2(dtv * q2);
+            av[0] = make_float2(a0, a0 * qv);
+            const float qsq = qv * qv;
+            const float2 qq = make_float2(qsq, qsq);
+#pragma unroll
+            for (int j = 1; j < NPR; ++j) av[j] = __fmul2_rn(av[j - 1], qq);
+            const float sc = u * rA0;
+            const float2 ss = make_float2(sc, sc), nss = make_float2(-sc, -sc);
+#pragma unroll
+            for (int j = 0; j < NPR; ++j) {
+                const float2 bj = make_float2(Bf[2 * j], Bf[2 * j + 1]);
+                const float2 w = __fmul2_rn(bj, ss), nw = __fmul2_rn(bj, nss);
+                hv[j] = __ffma2_rn(av[j], __fadd2_rn(hv[j], w), nw);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < NPR; ++j) av[j] = make_float2(ex2(dtv * A2[2 * j]), ex2(dtv * A2[2 * j + 1]));
+            const float2 uu = make_float2(u, u), dd = make_float2(dtv, dtv);
+#pragma unroll
+            for (int j = 0; j < NPR; ++j) {
+                // (A_bar - 1)/A as one fma; states with |A| < 1e-6 use dt instead
+                const float2 coef = __ffma2_rn(dd, lim2[j], __ffma2_rn(av[j], ci2[j], nci2[j]));
+                const float2 bu = __fmul2_rn(coef, __fmul2_rn(make_float2(Bf[2 * j], Bf[2 * j + 1]), uu));
+                hv[j] = __ffma2_rn(av[j], hv[j], bu);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NPR; ++j) { h[2 * j] = hv[j].x; h[2 * j + 1] = hv[j].y; }
+        float2 y0 = __fmul2_rn(make_float2(Cf[0], Cf[1]), hv[0]);
+        float2 y1 = __fmul2_rn(make_float2(Cf[2], Cf[3]), hv[1]);
+#pragma unroll
+        for (int j = 2; j < NPR; j += 2) {
+            y0 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y0);
+            y1 = __ffma2_rn(make_float2(Cf[2 * j + 2], Cf[2 * j + 3]), hv[j + 1], y1);
+        }
+        w_yp[tt * 128 + tid] = (y0.x + y0.y) + (y1.x + y1.y);
+        if (MODE == 1 && sub == 0) w_s[tt * CPB + cl] = u;
+    };
+
     const int nchunks = (int)((T_len + kTch - 1) / kTch);
     issue(0, raw_buf(0));
     for (int kc = 0; kc < nchunks; ++kc) {
@@ -260,85 +317,14 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         }
         if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
         __syncthreads();
-        // ---- recurrence ------------------------------------------------------
+        // ---- recurrence: a fixed-length, fully unrolled chunk ---------------------
         const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
-        auto step = [&](int tt, auto hip) {
-            constexpr bool HIP = decltype(hip)::value;
-            const float4* Bp = reinterpret_cast<const float4*>(w_B + tt * NP + sub * kNpt);
-            const float4* Cp = reinterpret_cast<const float4*>(w_C + tt * NP + sub * kNpt);
-            const float4 b0 = Bp[0], b1 = Bp[1], k0 = Cp[0], k1 = Cp[1];
-            const float2 Bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
-                                  make_float2(b1.z, b1.w)};
-            const float2 Cv[4] = {make_float2(k0.x, k0.y), make_float2(k0.z, k0.w), make_float2(k1.x, k1.y),
-                                  make_float2(k1.z, k1.w)};
-#pragma unroll
-            for (int k = 0; k < kCpt; ++k) {
-                const int cl = g + k * G;
-                float u;
-                if (MODE == 0) {
-                    u = w_u[tt * CPB + cl];
-                } else {
-                    // LIF step (snn.py:177-181) in fp32, identical in every thread of the channel
-                    mem[k] = __fadd_rn(__fmul_rn(beta[k], mem[k]), w_u[tt * CPB + cl]);
-                    u = (mem[k] >= th[k]) ? 1.f : 0.f;
-                    mem[k] = __fsub_rn(mem[k], __fmul_rn(th[k], u));
-                }
-                const float dtv = w_dt[tt * CPB + cl];
-                float2 av[kNpt / 2];
-                float2 hv[kNpt / 2];
-#pragma unroll
-                for (int j = 0; j < kNpt / 2; ++j) hv[j] = make_float2(h[k][2 * j], h[k][2 * j + 1]);
-                if (HIP) {
-                    // A[n] = (n+1) A0: exp(dt A[n]) by a chain of multiplies; the input
-                    // term uses w = u/A0 * B/(n+1): h' = A_bar (h + w) - w
-                    const float a0 = ex2(dtv * a2first[k]);
-                    const float qv = ex2(dtv * q2[k]);
-                    av[0] = make_float2(a0, a0 * qv);
-                    const float qsq = qv * qv;
-                    const float2 qq = make_float2(qsq, qsq);
-#pragma unroll
-                    for (int j = 1; j < kNpt / 2; ++j) av[j] = __fmul2_rn(av[j - 1], qq);
-                    const float sc = u * rA0[k];
-                    const float2 ss = make_float2(sc, sc);
-#pragma unroll
-                    for (int j = 0; j < kNpt / 2; ++j) {
-                        const float2 w = __fmul2_rn(Bv[j], ss);
-                        hv[j] = __ffma2_rn(av[j], __fadd2_rn(hv[j], w), make_float2(-w.x, -w.y));
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < kNpt / 2; ++j)
-                        av[j] = make_float2(ex2(dtv * A2[k][2 * j]), ex2(dtv * A2[k][2 * j + 1]));
-                    const float2 uu = make_float2(u, u);
-#pragma unroll
-                    for (int j = 0; j < kNpt / 2; ++j) {
-                        // (A_bar - 1)/A as one fma; states with |A| < 1e-6 use dt instead
-                        float2 coef = __ffma2_rn(av[j], make_float2(cinv[k][2 * j], cinv[k][2 * j + 1]),
-                                                 make_float2(-cinv[k][2 * j], -cinv[k][2 * j + 1]));
-                        if (lim_mask[k])
-                            coef = __ffma2_rn(make_float2(dtv, dtv),
-                                              make_float2((lim_mask[k] >> (2 * j)) & 1u ? 1.f : 0.f,
-                                                          (lim_mask[k] >> (2 * j + 1)) & 1u ? 1.f : 0.f), coef);
-                        const float2 bu = __fmul2_rn(coef, __fmul2_rn(Bv[j], uu));
-                        hv[j] = __ffma2_rn(av[j], hv[j], bu);
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < kNpt / 2; ++j) { h[k][2 * j] = hv[j].x; h[k][2 * j + 1] = hv[j].y; }
-                float2 y0 = __fmul2_rn(Cv[0], hv[0]);
-                float2 y1 = __fmul2_rn(Cv[1], hv[1]);
-                y0 = __ffma2_rn(Cv[2], hv[2], y0);
-                y1 = __ffma2_rn(Cv[3], hv[3], y1);
-                w_yp[(tt * kCpt + k) * 128 + tid] = (y0.x + y0.y) + (y1.x + y1.y);
-                if (MODE == 1 && sub == 0) w_s[tt * CPB + cl] = u;
-            }
-        };
         if (hippo) {
-#pragma unroll 2
-            for (int tt = 0; tt < nt; ++tt) step(tt, std::true_type{});
+#pragma unroll
+            for (int tt = 0; tt < kTch; ++tt) step(tt, nt, std::true_type{});
         } else {
-#pragma unroll 2
-            for (int tt = 0; tt < nt; ++tt) step(tt, std::false_type{});
+#pragma unroll
+            for (int tt = 0; tt < kTch; ++tt) step(tt, nt, std::false_type{});
         }
         __syncthreads();
         // ---- reduce partial sums, D*u, gate; coalesced stores -----------------
@@ -346,10 +332,9 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             const int tt = i / CPB, cc = i % CPB;
             const int64_t t = t0 + tt, cg = c0 + cc;
             if (tt >= nt || cg >= d) continue;
-            const int k = cc / G, gg = cc % G;
             float yp = 0.f;
 #pragma unroll
-            for (int s2 = 0; s2 < TPC; ++s2) yp += w_yp[(tt * kCpt + k) * 128 + gg * TPC + s2];
+            for (int s2 = 0; s2 < TPC; ++s2) yp += w_yp[tt * 128 + cc * TPC + s2];
             const float uu = MODE == 0 ? w_u[i] : w_s[i];
             const float yv = __fadd_rn(yp, __fmul_rn(w_D[cc], uu));
             int64_t row = row0 + t;
@@ -379,58 +364,74 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     }
     // ---- carry-out -----------------------------------------------------------
     void* sout = MODE ? (void*)f.state_out : a.state_out;
+    if (live && sout) {
 #pragma unroll
-    for (int k = 0; k < kCpt; ++k) {
-        if (!live[k]) continue;
-        if (sout) {
-#pragma unroll
-            for (int j = 0; j < kNpt; ++j) {
-                const int64_t n = (int64_t)sub * kNpt + j;
-                if (n >= N) continue;
-                const int64_t si = (b * d + ch[k]) * N + n;
-                if (MODE == 0 && SDT == NT_BF16) static_cast<__nv_bfloat16*>(sout)[si] = __float2bfloat16_rn(h[k][j]);
-                else static_cast<float*>(sout)[si] = h[k][j];
-            }
+        for (int j = 0; j < NPT; ++j) {
+            const int64_t n = (int64_t)sub * NPT + j;
+            if (n >= N) continue;
+            const int64_t si = (b * d + c) * N + n;
+            if (MODE == 0 && SDT == NT_BF16) static_cast<__nv_bfloat16*>(sout)[si] = __float2bfloat16_rn(h[j]);
+            else static_cast<float*>(sout)[si] = h[j];
         }
-        if (MODE == 1 && sub == 0 && f.mem_out) f.mem_out[b * d + ch[k]] = mem[k];
     }
-    if (MODE == 1 && f.spike_count) {
-        const unsigned w = __reduce_add_sync(0xffffffffu, spike_local);
-        if ((tid & 31) == 0 && w) atomicAdd(f.spike_count, (unsigned long long)w);
+    if (MODE == 1) {
+        if (live && sub == 0 && f.mem_out) f.mem_out[b * d + c] = mem;
+        if (f.spike_count) {
+            const unsigned w = __reduce_add_sync(0xffffffffu, spike_local);
+            if ((tid & 31) == 0 && w) atomicAdd(f.spike_count, (unsigned long long)w);
+        }
     }
 }
 
-int pow2_tpc(int64_t N) {
-    int tpc = 1;
-    while (tpc * kNpt < N) tpc <<= 1;
-    return tpc;
+int pow2_at_least(int64_t x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
 }
 
-template <int DT, int SDT, int MODE, int TPC>
+template <int DT, int SDT, int MODE, int TPC, int NPT>
 int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    const size_t smem = ScanSmem<TPC, T>::BYTES;
-    auto kern = ssm_scan_kernel<DT, SDT, TPC, MODE>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    using L = ScanSmem<TPC, NPT, T>;
+    auto kern = ssm_scan_kernel<DT, SDT, TPC, NPT, MODE>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
     const int64_t d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
-    constexpr int CPB = ScanSmem<TPC, T>::CPB;
-    dim3 grid((unsigned)((d + CPB - 1) / CPB), (unsigned)B);
-    kern<<<grid, 128, smem, stream>>>(a, f);
+    dim3 grid((unsigned)((d + L::CPB - 1) / L::CPB), (unsigned)B);
+    kern<<<grid, 128, L::BYTES, stream>>>(a, f);
     return check_launch("ssm_scan_kernel");
 }
 
+// States per thread: 8, or 4 when 8 would leave the GPU with fewer than four
+// 128-thread CTAs per SM (the recurrence is latency-bound, so warps matter
+// more than the extra per-thread work of a narrower state slice).
 template <int DT, int SDT, int MODE>
 int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
-    const int tpc = pow2_tpc(MODE ? f.N : a.N);
-    switch (tpc) {
-        case 1: return launch_tpc<DT, SDT, MODE, 1>(a, f, stream);
-        case 2: return launch_tpc<DT, SDT, MODE, 2>(a, f, stream);
-        case 4: return launch_tpc<DT, SDT, MODE, 4>(a, f, stream);
-        case 8: return launch_tpc<DT, SDT, MODE, 8>(a, f, stream);
-        case 16: return launch_tpc<DT, SDT, MODE, 16>(a, f, stream);
-        case 32: return launch_tpc<DT, SDT, MODE, 32>(a, f, stream);
-        default: return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)(MODE ? f.N : a.N));
+    const int64_t N = MODE ? f.N : a.N, d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
+    if (N > 256) return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)N);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tpc8 = pow2_at_least((N + 7) / 8);
+    const int64_t ctas8 = B * ((d + 128 / tpc8 - 1) / (128 / tpc8));
+    const bool narrow = N >= 8 && tpc8 <= 16 && ctas8 < 4LL * sms;
+    if (narrow) {
+        switch (pow2_at_least((N + 3) / 4)) {
+            case 2: return launch_tpc<DT, SDT, MODE, 2, 4>(a, f, stream);
+            case 4: return launch_tpc<DT, SDT, MODE, 4, 4>(a, f, stream);
+            case 8: return launch_tpc<DT, SDT, MODE, 8, 4>(a, f, stream);
+            case 16: return launch_tpc<DT, SDT, MODE, 16, 4>(a, f, stream);
+            case 32: return launch_tpc<DT, SDT, MODE, 32, 4>(a, f, stream);
+            default: break;
+        }
+    }
+    switch (tpc8) {
+        case 1: return launch_tpc<DT, SDT, MODE, 1, 8>(a, f, stream);
+        case 2: return launch_tpc<DT, SDT, MODE, 2, 8>(a, f, stream);
+        case 4: return launch_tpc<DT, SDT, MODE, 4, 8>(a, f, stream);
+        case 8: return launch_tpc<DT, SDT, MODE, 8, 8>(a, f, stream);
+        case 16: return launch_tpc<DT, SDT, MODE, 16, 8>(a, f, stream);
+        case 32: return launch_tpc<DT, SDT, MODE, 32, 8>(a, f, stream);
+        default: return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)N);
     }
 }
 

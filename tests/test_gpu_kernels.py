@@ -125,6 +125,18 @@ def test_selective_scan_fp32_vs_oracle(nat, Nst, hippo):
     np.testing.assert_allclose(N(so), rs, rtol=1e-4, atol=1e-6)
 
 
+@pytest.mark.parametrize("hippo", [True, False])
+def test_selective_scan_wide_batch(nat, hippo):
+    """Enough (batch, channel) pairs to fill the GPU: the 8-states-per-thread
+    configuration (the narrow 4-state one is covered by the small cases)."""
+    rng = np.random.default_rng(77 + hippo)
+    u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, 8, 45, 4096, 32, hippo=hippo)
+    y, so = nat.selective_scan(T(u), T(dt), T(Bm), T(Cm), T(log_A), T(D), T(st))
+    ry, rs = O.ssm_scan(u, dt, Bm, Cm, log_A, D, st, "fp32")
+    np.testing.assert_allclose(N(y), ry, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(N(so), rs, rtol=1e-4, atol=1e-6)
+
+
 def test_selective_scan_general_input_and_T1(nat):
     """Non-binary u (the layer accepts any input, tests/test_model.py:141) and T = 1."""
     rng = np.random.default_rng(5)

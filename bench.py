@@ -323,16 +323,100 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def _time_device(fn, steps, warmup, dev):
+    """Average device time (ms) of fn over `steps` calls, L2 flushed before each."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize(dev)
+    for a, b in evs:
+        flush.zero_()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+
+def run_standalone(args):
+    """Standalone ops of the path on one GPU (no torchrun):
+    fused-op:   LIF -> selective scan, B=16 x L=4096, d_inner 2304, d_state 64 (bf16 in, fp32 state)
+    sparse-out: spike-sparse out_proj, 32768 rows x K=4096 -> 2048, row activity 10/25/50%"""
+    import torch
+    from neuratensor_b200 import native
+    native.load()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    bf = torch.bfloat16
+    peak, kind = _peaks()
+    lines = []
+    if args.workload == "fused-op":
+        B, L, D, N = 16, 4096, 2304, 64
+        x = torch.randn(B, L, D, generator=g, device=dev).to(bf)
+        delta = torch.nn.functional.softplus(torch.randn(B, L, D, generator=g, device=dev) - 2.0).to(bf)
+        Bm = (torch.randn(B, L, N, generator=g, device=dev) / N ** 0.5).to(bf)
+        Cm = (torch.randn(B, L, N, generator=g, device=dev) / N ** 0.5).to(bf)
+        log_A = torch.log(torch.arange(1, N + 1, device=dev, dtype=torch.float32)).expand(D, N).contiguous()
+        Dsk = torch.ones(D, device=dev)
+        beta = torch.rand(D, generator=g, device=dev) * 0.19 + 0.80
+        th = torch.ones(D, device=dev)
+        mem0 = torch.randn(B, D, generator=g, device=dev) * 0.5
+        st0 = torch.randn(B, D, N, generator=g, device=dev) * 0.1
+        cnt = torch.zeros((), dtype=torch.int64, device=dev)
+        fn = lambda: native.lif_ssm_fused(x, delta, Bm, Cm, log_A, Dsk, beta, th, mem0, st0, spike_count=cnt)
+        ms = _time_device(fn, args.steps, args.warmup, dev)
+        algo = 1092911104
+        gbs = algo / (ms * 1e-3) / 1e9
+        lines.append({"metric": "tokens/s", "value": B * L / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "dtype": "bf16 in / fp32 state", "data": "synthetic (seeded)",
+                      "config": {"workload": "fused LIF+selective scan, B=16 L=4096 d=2304 N=64"},
+                      "roofline": {"kernel": "ssm_scan_kernel (LIF fused)", "bound": "hbm", "achieved": gbs,
+                                   "peak": peak, "unit": "GB/s", "frac": gbs / peak, "traffic": None,
+                                   "algorithmic_bytes": algo, "peak_source": kind},
+                      "state_updates_per_s": B * L * D * N / (ms * 1e-3)})
+    else:
+        M, K, Nout = 32768, 4096, 2048
+        o = torch.randn(M, K, generator=g, device=dev).to(bf)
+        W = (torch.randn(Nout, K, generator=g, device=dev) * 0.02).to(bf)
+        for p in (0.10, 0.25, 0.50):
+            act = torch.rand(M, generator=g, device=dev) < p
+            spk = ((torch.rand(M, K, generator=g, device=dev) < 0.2) & act[:, None]).to(bf)
+            n_act = int(spk.any(-1).sum().item())
+            fn = lambda: native.sparse_out_proj(o, spk, W)
+            ms = _time_device(fn, args.steps, args.warmup, dev)
+            dense = 2 * n_act > M
+            rows = M if dense else n_act
+            flops = 2.0 * rows * K * Nout
+            byts = M * K * 2 + rows * K * 2 + K * Nout * 2 + M * Nout * 2
+            lines.append({"metric": "rows/s", "value": M / (ms * 1e-3), "unit": "rows/s", "n_gpus": 1,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                          "dtype": "bf16", "data": "synthetic (seeded)",
+                          "config": {"workload": f"sparse out_proj M={M} K={K} N={Nout} p={p}", "n_active": n_act,
+                                     "branch": "dense" if dense else "sparse"},
+                          "tflops": flops / (ms * 1e-3) / 1e12, "gbs": byts / (ms * 1e-3) / 1e9,
+                          "algorithmic_bytes": byts, "flops": flops})
+    for ln in lines:
+        print(json.dumps(ln), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="model", choices=["model", "fused-op", "sparse-out"],
+                    help="model: small-preset prefill (the headline); the others time one op")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "model":
+        run_standalone(args)
     else:
         run_ours(args)
 

@@ -25,8 +25,8 @@
 //   y     = sum_n C[n]*h[n] + D*u
 // HiPPO fast path: when A[c,n] = (n+1)*A[c,0] for every state of every
 // channel of the CTA (the reference's initialisation, ssm.py:34-43), a
-// thread needs two exponentials per step and a chain of multiplies:
-// exp(dt*A[c,n+1]) = exp(dt*A[c,n]) * exp(dt*A[c,0]).  The structure test is
+// thread needs two exponentials per step and a chain of fmas:
+// exp(dt*A[c,n+1]) = exp(dt*A[c,n]) * exp(dt*A[c,0]), carried as e = A_bar - 1.  The structure test is
 // 1e-6 relative on A for float32 parameters; for bfloat16 parameters it is
 // made on log_A (one bf16 ulp of log(n+1) + log_A[c,0]), because a bf16 model
 // stores log(n+1) rounded and exp() of that lands up to ~2% away from n+1.
@@ -83,16 +83,6 @@ __device__ __forceinline__ void stage_tile(T* dst, const T* src, int64_t ld, int
     }
 }
 
-// f(std::integral_constant<int, 0>) ... f(std::integral_constant<int, N-1>): a
-// compile-time unrolled loop (every index is a constant in the body).
-template <int I, int N, typename F>
-__device__ __forceinline__ void static_for(F&& f) {
-    if constexpr (I < N) {
-        f(std::integral_constant<int, I>{});
-        static_for<I + 1, N>(f);
-    }
-}
-
 template <int TPC, int NPT, typename T>
 struct ScanSmem {
     // time steps per staged chunk (halved where the channel or state tile is widest)
@@ -101,7 +91,7 @@ struct ScanSmem {
     static constexpr int NP = NPT * TPC;                // padded d_state
     static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;       // elements of T per staging buffer
     static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
-    static constexpr int WORK_FLOATS = 4 * TCH * CPB + 2 * TCH * NP + TCH * 128 + TCH * CPB + 3 * CPB + TCH;
+    static constexpr int WORK_FLOATS = 2 * TCH * CPB + 2 * TCH * NP + TCH * 128 + TCH * CPB + CPB + NP + TCH;
     static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + sizeof(float) * (size_t)WORK_FLOATS;
 };
 
@@ -120,12 +110,9 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     float* w_C = w_B + kTch * NP;                                        // [kTch][NP]
     float* w_yp = w_C + kTch * NP;                                       // [kTch][128] partial C.h
     float* w_s = w_yp + kTch * 128;                                      // [kTch][CPB] spikes (MODE 1)
-    float* w_q = w_s + kTch * CPB;                                       // [kTch][CPB] exp(dt*A0) (HiPPO)
-    float* w_sc = w_q + kTch * CPB;                                      // [kTch][CPB] u/A0 (HiPPO)
-    float* w_D = w_sc + kTch * CPB;                                      // [CPB] skip weights D
-    float* w_q2 = w_D + CPB;                                             // [CPB] A0*log2(e)
-    float* w_rA0 = w_q2 + CPB;                                           // [CPB] 1/A0
-    int* w_pos = reinterpret_cast<int*>(w_rA0 + CPB);                    // [kTch] compacted row positions
+    float* w_D = w_s + kTch * CPB;                                       // [CPB] skip weights D
+    float* w_rn = w_D + CPB;                                             // [NP] 1/(n+1)
+    int* w_pos = reinterpret_cast<int*>(w_rn + NP);                      // [kTch] compacted row positions
 
     const int64_t T_len = MODE ? f.L : a.T, d = MODE ? f.d : a.d, N = MODE ? f.N : a.N;
     const T* p_u = static_cast<const T*>(MODE ? f.x : a.u);
@@ -188,7 +175,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     }
     const bool hippo = __syncthreads_and(hippo_ok ? 1 : 0) != 0;
     // HiPPO constants: first-state exponent, ratio exponent, 1/A[c,0]
-    const float kfirst = (float)(sub * NPT + 1);        // first state's exponent in units of dt*A0
+    const float a2first = (float)(sub * NPT + 1) * Abase * kLog2e;
     const float q2 = Abase * kLog2e;
     const float rA0 = 1.0f / Abase;
     float2 ci2[NPR], nci2[NPR], lim2[NPR];
@@ -204,14 +191,11 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         th = f.threshold[c];
         if (f.mem_in) mem = f.mem_in[b * d + c];
     }
+    for (int i = tid; i < NP; i += 128) w_rn[i] = 1.0f / (float)(i + 1);
     for (int i = tid; i < CPB; i += 128) {
         const int64_t cg = c0 + i;
         w_D[i] = cg < d ? (MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + cg) : f.Dskip[cg])
                         : 0.f;
-    }
-    if (sub == 0) {
-        w_q2[cl] = q2;
-        w_rA0[cl] = rA0;
     }
     unsigned spike_local = 0;
     const bool sparse_rows = (MODE == 0) && a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
@@ -264,27 +248,29 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             u = in_seq ? s1 : 0.f;
             mem = in_seq ? m2 : mem;
         }
-        const float dtv = w_dt[tt * CPB + cl];    // L = dt*A0*log2(e) on the HiPPO path
+        const float dtv = w_dt[tt * CPB + cl];
         float2 av[NPR], hv[NPR];
 #pragma unroll
         for (int j = 0; j < NPR; ++j) hv[j] = make_float2(h[2 * j], h[2 * j + 1]);
         if (HIP) {
-            // A[n] = (n+1) A0: exp(dt A[n]) by a chain of multiplies; the input term
-            // uses w = u/A0 * B/(n+1):  h' = A_bar (h + w) - w
-            const float a0 = ex2(dtv * kfirst);
-            const float qv = w_q[tt * CPB + cl];
-            av[0] = make_float2(a0, a0 * qv);
-            const float qsq = qv * qv;
-            const float2 qq = make_float2(qsq, qsq);
+            // A[n] = (n+1) A0.  With e = A_bar - 1 = exp(dt A[n]) - 1 and
+            // w = u/A0 * B/(n+1) = u * B_bar / e, the update A_bar h + B_bar u is
+            //     h' = h + e (h + w)
+            // and e follows the chain e[n+1] = e[n] q + (q - 1), q = exp(dt A0).
+            const float e0 = ex2(dtv * a2first) - 1.0f;
+            const float qv = ex2(dtv * q2);
+            av[0] = make_float2(e0, __fmaf_rn(e0, qv, qv - 1.0f));
+            const float2 qq = make_float2(qv * qv, qv * qv);
+            const float qm = __fmaf_rn(qv, qv, -1.0f);
+            const float2 qqm = make_float2(qm, qm);
 #pragma unroll
-            for (int j = 1; j < NPR; ++j) av[j] = __fmul2_rn(av[j - 1], qq);
-            const float sc = MODE == 0 ? w_sc[tt * CPB + cl] : u * rA0;   // fused op: u is this step's spike
-            const float2 ss = make_float2(sc, sc), nss = make_float2(-sc, -sc);
+            for (int j = 1; j < NPR; ++j) av[j] = __ffma2_rn(av[j - 1], qq, qqm);
+            const float sc = u * rA0;
+            const float2 ss = make_float2(sc, sc);
 #pragma unroll
             for (int j = 0; j < NPR; ++j) {
-                const float2 bj = make_float2(Bf[2 * j], Bf[2 * j + 1]);
-                const float2 w = __fmul2_rn(bj, ss), nw = __fmul2_rn(bj, nss);
-                hv[j] = __ffma2_rn(av[j], __fadd2_rn(hv[j], w), nw);
+                const float2 w = __fmul2_rn(make_float2(Bf[2 * j], Bf[2 * j + 1]), ss);
+                hv[j] = __ffma2_rn(av[j], __fadd2_rn(hv[j], w), hv[j]);
             }
         } else {
 #pragma unroll
@@ -307,9 +293,8 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             y0 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y0);
             y1 = __ffma2_rn(make_float2(Cf[2 * j + 2], Cf[2 * j + 3]), hv[j + 1], y1);
         }
-        const float2 ys = __fadd2_rn(y0, y1);
-        w_yp[tt * 128 + tid] = ys.x + ys.y;
-        if (MODE == 1 && sub == 0) w_s[tt * CPB + cl] = u;
+        w_yp[tt * 128 + tid] = (y0.x + y0.y) + (y1.x + y1.y);
+        if (MODE == 1) w_s[tt * CPB + cl] = u;   // every thread of the channel stores the same value
     };
 
     const int nchunks = (int)((T_len + kTch - 1) / kTch);
@@ -326,31 +311,25 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         // ---- widen the chunk to float32 (B pre-divided by n+1 on the HiPPO path)
         const T* rb = raw_buf(kc);
         for (int i = tid; i < kTch * CPB; i += 128) {
-            const float uv = to_f(rb[i]), dv = to_f(rb[kTch * CPB + i]);
-            w_u[i] = uv;
-            if (hippo) {
-                // per (step, channel), shared by the channel's TPC threads:
-                // L = dt*A0*log2(e), q = exp(dt*A0), sc = u/A0
-                const int cc = i % CPB;
-                const float Lv = dv * w_q2[cc];
-                w_dt[i] = Lv;
-                w_q[i] = ex2(Lv);
-                w_sc[i] = uv * w_rA0[cc];
-            } else {
-                w_dt[i] = dv;
-            }
+            w_u[i] = to_f(rb[i]);
+            w_dt[i] = to_f(rb[kTch * CPB + i]);
         }
         for (int i = tid; i < kTch * NP; i += 128) {
             const float bv = to_f(rb[3 * kTch * CPB + i]);
-            w_B[i] = hippo ? __fdiv_rn(bv, (float)(i % NP + 1)) : bv;
+            w_B[i] = hippo ? bv * w_rn[i % NP] : bv;
             w_C[i] = to_f(rb[3 * kTch * CPB + kTch * NP + i]);
         }
         if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
         __syncthreads();
         // ---- recurrence: a fixed-length, fully unrolled chunk ---------------------
         const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
-        if (hippo) static_for<0, kTch>([&](auto tt) { step(decltype(tt)::value, nt, std::true_type{}); });
-        else static_for<0, kTch>([&](auto tt) { step(decltype(tt)::value, nt, std::false_type{}); });
+        if (hippo) {
+#pragma unroll
+            for (int tt = 0; tt < kTch; ++tt) step(tt, nt, std::true_type{});
+        } else {
+#pragma unroll
+            for (int tt = 0; tt < kTch; ++tt) step(tt, nt, std::false_type{});
+        }
         __syncthreads();
         // ---- reduce partial sums, D*u, gate; coalesced stores -----------------
         for (int i = tid; i < kTch * CPB; i += 128) {

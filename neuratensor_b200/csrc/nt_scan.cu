@@ -83,10 +83,21 @@ __device__ __forceinline__ void stage_tile(T* dst, const T* src, int64_t ld, int
     }
 }
 
-template <int TPC, int NPT, typename T>
+// f(std::integral_constant<int, 0>) ... f(std::integral_constant<int, N-1>): a
+// compile-time unrolled loop (every index is a constant in the body).
+template <int I, int N, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+    if constexpr (I < N) {
+        f(std::integral_constant<int, I>{});
+        static_for<I + 1, N>(f);
+    }
+}
+
+template <int TPC, int NPT, typename T, int MODE>
 struct ScanSmem {
-    // time steps per staged chunk (halved where the channel or state tile is widest)
-    static constexpr int TCH = (TPC == 1 || TPC == 32) ? 16 : 32;
+    // time steps per staged chunk: 32, or 16 where the channel or state tile is
+    // widest and for the fused op (whose per-step spikes also live in registers)
+    static constexpr int TCH = (TPC == 1 || TPC == 32 || MODE == 1) ? 16 : 32;
     static constexpr int CPB = 128 / TPC;               // channels per CTA
     static constexpr int NP = NPT * TPC;                // padded d_state
     static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;       // elements of T per staging buffer
@@ -101,7 +112,7 @@ template <int DT, int SDT, int TPC, int NPT, int MODE>
 __global__ void __launch_bounds__(128)
 ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    using L = ScanSmem<TPC, NPT, T>;
+    using L = ScanSmem<TPC, NPT, T, MODE>;
     constexpr int CPB = L::CPB, NP = L::NP, kTch = L::TCH, NPR = NPT / 2;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float* w_u = reinterpret_cast<float*>(smem_raw + 2 * L::RAW_BYTES);  // [kTch][CPB] u (or x)
@@ -226,7 +237,11 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
 
     // one step; steps past the end of the sequence see u = dt = B = 0, which
     // leaves the state unchanged (A_bar = 1, no input term)
-    auto step = [&](int tt, int nt, auto hip) {
+    // One step.  The step's partial C.h (and, in MODE 1, its spike) go to
+    // registers; they reach shared memory only after the whole chunk, so no
+    // store sits between one step's loads and the next step's (the compiler can
+    // then overlap the independent exponentials and loads of successive steps).
+    auto step = [&](int tt, int nt, auto hip, float& yp_out, float& u_out) {
         constexpr bool HIP = decltype(hip)::value;
         float Bf[NPT], Cf[NPT];
 #pragma unroll
@@ -293,8 +308,8 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             y0 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y0);
             y1 = __ffma2_rn(make_float2(Cf[2 * j + 2], Cf[2 * j + 3]), hv[j + 1], y1);
         }
-        w_yp[tt * 128 + tid] = (y0.x + y0.y) + (y1.x + y1.y);
-        if (MODE == 1) w_s[tt * CPB + cl] = u;   // every thread of the channel stores the same value
+        yp_out = (y0.x + y0.y) + (y1.x + y1.y);
+        u_out = u;
     };
 
     const int nchunks = (int)((T_len + kTch - 1) / kTch);
@@ -323,12 +338,13 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         __syncthreads();
         // ---- recurrence: a fixed-length, fully unrolled chunk ---------------------
         const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
-        if (hippo) {
+        float ypr[kTch], upr[kTch];
+        if (hippo) static_for<0, kTch>([&](auto tt) { step(decltype(tt)::value, nt, std::true_type{}, ypr[decltype(tt)::value], upr[decltype(tt)::value]); });
+        else static_for<0, kTch>([&](auto tt) { step(decltype(tt)::value, nt, std::false_type{}, ypr[decltype(tt)::value], upr[decltype(tt)::value]); });
 #pragma unroll
-            for (int tt = 0; tt < kTch; ++tt) step(tt, nt, std::true_type{});
-        } else {
-#pragma unroll
-            for (int tt = 0; tt < kTch; ++tt) step(tt, nt, std::false_type{});
+        for (int tt = 0; tt < kTch; ++tt) {
+            w_yp[tt * 128 + tid] = ypr[tt];
+            if (MODE == 1) w_s[tt * CPB + cl] = upr[tt];   // every thread of the channel stores the same value
         }
         __syncthreads();
         // ---- reduce partial sums, D*u, gate; coalesced stores -----------------
@@ -396,7 +412,7 @@ int pow2_at_least(int64_t x) {
 template <int DT, int SDT, int MODE, int TPC, int NPT>
 int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    using L = ScanSmem<TPC, NPT, T>;
+    using L = ScanSmem<TPC, NPT, T, MODE>;
     auto kern = ssm_scan_kernel<DT, SDT, TPC, NPT, MODE>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));

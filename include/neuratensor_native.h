@@ -28,6 +28,7 @@
 #ifndef NEURATENSOR_NATIVE_H
 #define NEURATENSOR_NATIVE_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -130,6 +131,21 @@ NT_API int nt_rmsnorm_in_proj(int dtype, int64_t M, int64_t dm, int64_t di,
                        const void* x, const void* gamma, const void* W_in,
                        void* h, void* gate,
                        void* workspace, int64_t workspace_bytes, void* stream);
+
+/* RMSNorm + in_proj without a workspace (no counterpart in the reference).
+ * Same computation and arguments as nt_rmsnorm_in_proj, minus the workspace:
+ * the normalised activations go to a scratch array the library itself holds
+ * in device memory (nt_noalloc_scratch_bytes() bytes per device, 32 MiB), for
+ * callers that cannot allocate device memory, e.g. serving runtimes that
+ * reserve HBM at start-up and forbid cudaMalloc afterwards.  Requires
+ * M*d_model*sizeof(dtype) <= nt_noalloc_scratch_bytes() (else NT_ERR_ARG).
+ * The first call on a device, made with that device current, looks up the
+ * array's address; make it before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race. */
+NT_API size_t nt_noalloc_scratch_bytes(void);
+NT_API int nt_rmsnorm_in_proj_noalloc(int dtype, int64_t M, int64_t dm, int64_t di,
+                       const void* x, const void* gamma, const void* W_in,
+                       void* h, void* gate, void* stream);
 
 /* FusedSpikeBlock.forward in eval mode (fused.py:101-147):
  *   out = sparse_out_proj(SSM(LIF(in_proj(RMSNorm(x))_h)) * silu(gate)) * out_scale + x

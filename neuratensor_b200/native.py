@@ -48,6 +48,8 @@ _SIGS = {
     "nt_sparse_out_proj": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _P], _I32),
     "nt_rmsnorm_in_proj_workspace_bytes": ([_I32, _I64, _I64, _I64], _I64),
     "nt_rmsnorm_in_proj": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _P], _I32),
+    "nt_noalloc_scratch_bytes": ([], ctypes.c_size_t),
+    "nt_rmsnorm_in_proj_noalloc": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P], _I32),
     "nt_block_workspace_bytes": ([_I32, _I64, _I64, _I64, _I64, _I64], _I64),
     "nt_block_forward": ([_I32, _I32, _I64, _I64, _I64, _I64, _I64] + [_P] * 17 + [_I32, _P, _I64, _P], _I32),
     "nt_lif_ssm_fused": ([_I64, _I64, _I64, _I64] + [_P] * 14 + [_I32, _P, _P], _I32),
@@ -241,6 +243,23 @@ def rmsnorm_in_proj(x: Tensor, gamma: Tensor, W_in: Tensor) -> Tuple[Tensor, Ten
     rc = L.nt_rmsnorm_in_proj(_DT[a], M, dm, di, _p(x2), _p(g2), _p(W2), _p(h), _p(gate), _p(ws), nbytes,
                               _stream(dev))
     _check("nt_rmsnorm_in_proj", rc)
+    return h, gate
+
+
+def rmsnorm_in_proj_noalloc(x: Tensor, gamma: Tensor, W_in: Tensor) -> Tuple[Tensor, Tensor]:
+    """rmsnorm_in_proj without a workspace: for callers that cannot allocate device
+    memory at call time; the library's own static scratch holds the normalised rows
+    (at most nt_noalloc_scratch_bytes() of them).  Calls overlapping on the GPU race."""
+    dev = _require_cuda(x, gamma, W_in)
+    a = x.dtype
+    dm = x.shape[-1]
+    di = W_in.shape[0] // 2
+    M = x.numel() // dm
+    x2, g2, W2 = _c(x), _c(gamma, a), _c(W_in, a)
+    h = torch.empty((*x.shape[:-1], di), dtype=a, device=dev)
+    gate = torch.empty_like(h)
+    rc = load().nt_rmsnorm_in_proj_noalloc(_DT[a], M, dm, di, _p(x2), _p(g2), _p(W2), _p(h), _p(gate), _stream(dev))
+    _check("nt_rmsnorm_in_proj_noalloc", rc)
     return h, gate
 
 

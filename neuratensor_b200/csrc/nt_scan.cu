@@ -102,14 +102,68 @@ struct ScanSmem {
     static constexpr int NP = NPT * TPC;                // padded d_state
     static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;       // elements of T per staging buffer
     static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
-    static constexpr int WORK_FLOATS = 2 * TCH * CPB + 2 * TCH * NP + TCH * 128 + TCH * CPB + CPB + NP + TCH;
+    // partial-sum row pitch: 128 slots, plus CPB when a warp's reduction loads
+    // span several steps (their rows then start in different banks)
+    static constexpr int YS = 128 + (CPB < 32 ? CPB : 0);
+    static constexpr int WORK_FLOATS =
+        2 * TCH * CPB + 2 * TCH * NP + TCH * YS + (MODE == 1 ? TCH * CPB : 0) + CPB + NP + TCH;
     static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + sizeof(float) * (size_t)WORK_FLOATS;
 };
 
+// Slot of the partial C.h sum of (sub s, channel c) within a step's row of
+// the partial-sum buffer (row pitch ScanSmem::YS).  Sub s owns CPB slots and
+// channel c sits at c ^ X(s): the 32 stores of a warp (32/TPC channels x TPC
+// subs, one step) fall in 32 distinct banks, and so do the reduction's loads
+// (consecutive channels of 32/CPB consecutive steps, one sub), whose rows the
+// pitch YS = 128 + CPB shifts by CPB banks each.
+template <int TPC>
+__device__ __forceinline__ int yp_slot(int s, int c) {
+    constexpr int CPB = 128 / TPC;
+    int x = 0;
+    if constexpr (TPC == 2) x = 16 * s;
+    else if constexpr (TPC >= 4) x = (32 / TPC) * (s / (TPC / 4));
+    return s * CPB + (c ^ x);
+}
+
+// Position of state n within a staged B or C row.  Rows of 64 or more states
+// swap float4 pairs in every other group of eight float4s, so that the eight
+// threads of a quarter-warp reading two float4s each (8 states per thread)
+// hit distinct banks; groups of four states stay contiguous.
+template <int NP>
+__device__ __forceinline__ int bc_swz(int n) {
+    if constexpr (NP >= 64) return n ^ (((n >> 5) & 1) << 2);
+    else return n;
+}
+
+// Widen EPV = 16/sizeof(T) elements (one 16-byte vector) to float32.
+__device__ __forceinline__ void widen16(const float* src, float* v) {
+    const float4 q = *reinterpret_cast<const float4*>(src);
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void widen16(const __nv_bfloat16* src, float* v) {
+    const uint4 q = *reinterpret_cast<const uint4*>(src);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+}
+
 // MODE 0: selective scan with given u.  MODE 1: u = LIF spikes of x (fused op).
 // Thread (cl, sub) owns states [NPT*sub, NPT*sub + NPT) of channel c0 + cl.
+#ifndef NT_SCAN_MINB8
+#define NT_SCAN_MINB8 4
+#endif
+#ifndef NT_SCAN_MINB4
+#define NT_SCAN_MINB4 5
+#endif
+// Resident CTAs per SM the register allocation must allow (the recurrence is
+// latency-bound, so warps per SM matter more than hoisting further ahead).
+template <int NPT> struct ScanMinBlocks { static constexpr int value = NPT == 8 ? NT_SCAN_MINB8 : NT_SCAN_MINB4; };
+
 template <int DT, int SDT, int TPC, int NPT, int MODE>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, ScanMinBlocks<NPT>::value)
 ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
     using L = ScanSmem<TPC, NPT, T, MODE>;
@@ -119,9 +173,9 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     float* w_dt = w_u + kTch * CPB;                                      // [kTch][CPB]
     float* w_B = w_dt + kTch * CPB;                                      // [kTch][NP]  B (or B/(n+1))
     float* w_C = w_B + kTch * NP;                                        // [kTch][NP]
-    float* w_yp = w_C + kTch * NP;                                       // [kTch][128] partial C.h
-    float* w_s = w_yp + kTch * 128;                                      // [kTch][CPB] spikes (MODE 1)
-    float* w_D = w_s + kTch * CPB;                                       // [CPB] skip weights D
+    float* w_yp = w_C + kTch * NP;                                       // [kTch][YS] partial C.h (yp_slot)
+    float* w_s = w_yp + kTch * L::YS;                                    // [kTch][CPB] spikes (MODE 1 only)
+    float* w_D = w_s + (MODE == 1 ? kTch * CPB : 0);                     // [CPB] skip weights D
     float* w_rn = w_D + CPB;                                             // [NP] 1/(n+1)
     int* w_pos = reinterpret_cast<int*>(w_rn + NP);                      // [kTch] compacted row positions
 
@@ -246,8 +300,9 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         float Bf[NPT], Cf[NPT];
 #pragma unroll
         for (int q = 0; q < NPT / 4; ++q) {
-            const float4 bq = reinterpret_cast<const float4*>(w_B + tt * NP + sub * NPT)[q];
-            const float4 cq = reinterpret_cast<const float4*>(w_C + tt * NP + sub * NPT)[q];
+            const int n4 = bc_swz<NP>(sub * NPT + 4 * q);
+            const float4 bq = *reinterpret_cast<const float4*>(w_B + tt * NP + n4);
+            const float4 cq = *reinterpret_cast<const float4*>(w_C + tt * NP + n4);
             Bf[4 * q] = bq.x; Bf[4 * q + 1] = bq.y; Bf[4 * q + 2] = bq.z; Bf[4 * q + 3] = bq.w;
             Cf[4 * q] = cq.x; Cf[4 * q + 1] = cq.y; Cf[4 * q + 2] = cq.z; Cf[4 * q + 3] = cq.w;
         }
@@ -270,7 +325,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         if (HIP) {
             // A[n] = (n+1) A0.  With e = A_bar - 1 = exp(dt A[n]) - 1 and
             // w = u/A0 * B/(n+1) = u * B_bar / e, the update A_bar h + B_bar u is
-            //     h' = h + e (h + w)
+            //     h' = h + e (h + w)      (two fmas: t = B/(n+1) * u/A0 + h, h + e t)
             // and e follows the chain e[n+1] = e[n] q + (q - 1), q = exp(dt A0).
             const float e0 = ex2(dtv * a2first) - 1.0f;
             const float qv = ex2(dtv * q2);
@@ -284,8 +339,8 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             const float2 ss = make_float2(sc, sc);
 #pragma unroll
             for (int j = 0; j < NPR; ++j) {
-                const float2 w = __fmul2_rn(make_float2(Bf[2 * j], Bf[2 * j + 1]), ss);
-                hv[j] = __ffma2_rn(av[j], __fadd2_rn(hv[j], w), hv[j]);
+                const float2 t = __ffma2_rn(make_float2(Bf[2 * j], Bf[2 * j + 1]), ss, hv[j]);
+                hv[j] = __ffma2_rn(av[j], t, hv[j]);
             }
         } else {
 #pragma unroll
@@ -325,36 +380,59 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         __syncthreads();
         // ---- widen the chunk to float32 (B pre-divided by n+1 on the HiPPO path)
         const T* rb = raw_buf(kc);
-        for (int i = tid; i < kTch * CPB; i += 128) {
-            w_u[i] = to_f(rb[i]);
-            w_dt[i] = to_f(rb[kTch * CPB + i]);
+        for (int i = tid * EPV; i < kTch * CPB; i += 128 * EPV) {
+            float v[EPV];
+            widen16(rb + i, v);
+#pragma unroll
+            for (int k = 0; k < EPV; k += 4) *reinterpret_cast<float4*>(w_u + i + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+            widen16(rb + kTch * CPB + i, v);
+#pragma unroll
+            for (int k = 0; k < EPV; k += 4) *reinterpret_cast<float4*>(w_dt + i + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
         }
-        for (int i = tid; i < kTch * NP; i += 128) {
-            const float bv = to_f(rb[3 * kTch * CPB + i]);
-            w_B[i] = hippo ? bv * w_rn[i % NP] : bv;
-            w_C[i] = to_f(rb[3 * kTch * CPB + kTch * NP + i]);
+        for (int i = tid * EPV; i < kTch * NP; i += 128 * EPV) {
+            float bv[EPV], cv[EPV];
+            widen16(rb + 3 * kTch * CPB + i, bv);
+            widen16(rb + 3 * kTch * CPB + kTch * NP + i, cv);
+#pragma unroll
+            for (int k = 0; k < EPV; k += 4) {
+                const int tt = (i + k) / NP, n = (i + k) % NP;     // four states of one row
+                const int o = tt * NP + bc_swz<NP>(n);
+                float4 b4 = make_float4(bv[k], bv[k + 1], bv[k + 2], bv[k + 3]);
+                if (hippo) { b4.x *= w_rn[n]; b4.y *= w_rn[n + 1]; b4.z *= w_rn[n + 2]; b4.w *= w_rn[n + 3]; }
+                *reinterpret_cast<float4*>(w_B + o) = b4;
+                *reinterpret_cast<float4*>(w_C + o) = make_float4(cv[k], cv[k + 1], cv[k + 2], cv[k + 3]);
+            }
         }
         if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
         __syncthreads();
-        // ---- recurrence: a fixed-length, fully unrolled chunk ---------------------
+        // ---- recurrence: fixed-length, fully unrolled runs of kRun steps --------
+        // (each run's partial sums stay in registers and are stored after it)
         const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
-        float ypr[kTch], upr[kTch];
-        if (hippo) static_for<0, kTch>([&](auto tt) { step(decltype(tt)::value, nt, std::true_type{}, ypr[decltype(tt)::value], upr[decltype(tt)::value]); });
-        else static_for<0, kTch>([&](auto tt) { step(decltype(tt)::value, nt, std::false_type{}, ypr[decltype(tt)::value], upr[decltype(tt)::value]); });
+        constexpr int kRun = kTch < 16 ? kTch : 16;
+        static_for<0, kTch / kRun>([&](auto run) {
+            constexpr int r0 = decltype(run)::value * kRun;
+            float ypr[kRun], upr[kRun];
+            if (hippo) static_for<0, kRun>([&](auto j) { constexpr int q = decltype(j)::value; step(r0 + q, nt, std::true_type{}, ypr[q], upr[q]); });
+            else static_for<0, kRun>([&](auto j) { constexpr int q = decltype(j)::value; step(r0 + q, nt, std::false_type{}, ypr[q], upr[q]); });
 #pragma unroll
-        for (int tt = 0; tt < kTch; ++tt) {
-            w_yp[tt * 128 + tid] = ypr[tt];
-            if (MODE == 1) w_s[tt * CPB + cl] = upr[tt];   // every thread of the channel stores the same value
-        }
+            for (int q = 0; q < kRun; ++q) {
+                w_yp[(r0 + q) * L::YS + yp_slot<TPC>(sub, cl)] = ypr[q];
+                if (MODE == 1) w_s[(r0 + q) * CPB + cl] = upr[q];   // every thread of the channel stores the same value
+            }
+        });
         __syncthreads();
         // ---- reduce partial sums, D*u, gate; coalesced stores -----------------
-        for (int i = tid; i < kTch * CPB; i += 128) {
-            const int tt = i / CPB, cc = i % CPB;
+        // thread tid covers channel tid % CPB of steps tid / CPB + k*TPC
+#pragma unroll 1
+        for (int k = 0; k < (kTch * CPB + 127) / 128; ++k) {
+            const int i = tid + 128 * k;
+            if ((kTch * CPB) % 128 != 0 && i >= kTch * CPB) break;
+            const int tt = tid / CPB + k * TPC, cc = tid % CPB;
             const int64_t t = t0 + tt, cg = c0 + cc;
             if (tt >= nt || cg >= d) continue;
             float yp = 0.f;
 #pragma unroll
-            for (int s2 = 0; s2 < TPC; ++s2) yp += w_yp[tt * 128 + cc * TPC + s2];
+            for (int s2 = 0; s2 < TPC; ++s2) yp += w_yp[tt * L::YS + yp_slot<TPC>(s2, cc)];
             const float uu = MODE == 0 ? w_u[i] : w_s[i];
             const float yv = __fadd_rn(yp, __fmul_rn(w_D[cc], uu));
             int64_t row = row0 + t;

@@ -1,11 +1,13 @@
 // GEMMs of the block: D[M,N] = A[M,K] * W[N,K]^T with fused epilogues.
 //
-//  * bf16: a tcgen05 tensor-core kernel.  TMA (cp.async.bulk.tensor, 128-byte
-//    swizzle) streams A and W tiles into a STAGES-deep shared-memory ring;
-//    one elected thread issues tcgen05.mma (kind::f16, fp32 accumulation in
-//    TMEM); four epilogue warps read the 128 x BN accumulator back with
-//    tcgen05.ld and apply the epilogue (softplus for dt, out_scale +
-//    residual + row scatter for out_proj, ...).
+//  * bf16: a persistent tcgen05 tensor-core kernel, one CTA per SM walking
+//    128 x BN output tiles.  A TMA warp (cp.async.bulk.tensor, 128-byte
+//    swizzle) streams A and W k-blocks into a STAGES-deep shared-memory ring;
+//    one elected thread of the MMA warp issues tcgen05.mma (kind::f16, fp32
+//    accumulation) into one of two TMEM accumulators; eight epilogue warps
+//    drain the other accumulator with tcgen05.ld and apply the epilogue
+//    (softplus for dt, out_scale + residual + row scatter for out_proj, ...),
+//    so a tile's epilogue overlaps the next tile's MMAs.
 //  * fp32: the reference's fp32 mode needs fp32 products; a tiled CUDA-core
 //    kernel with the same epilogues.
 //
@@ -21,6 +23,19 @@ namespace nt {
 // ---------------------------------------------------------------------------
 // Epilogue (per element; rounding points follow the reference's tensor ops)
 // ---------------------------------------------------------------------------
+
+// softplus(v) = max(v, 0) + log1p(exp(-|v|)), identity above 20 (the
+// reference's threshold, ssm.py:330).  exp and log on the MUFU pipe; log1p(z)
+// for z < 1e-2 from its Taylor series z - z^2/2 + z^3/3, where log(1 + z)
+// would lose the low bits of z.
+__device__ __forceinline__ float softplus_f(float v) {
+    if (v > 20.f) return v;
+    const float z = __expf(-fabsf(v));
+    const float l = z < 1e-2f ? z * (1.f - z * (0.5f - z * (1.f / 3.f))) : __logf(1.f + z);
+    return fmaxf(v, 0.f) + l;
+}
+// silu(g) = g * sigmoid(g)
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 template <int DT, int KIND>
 __device__ __forceinline__ void epi_apply(const EpiArgs& e, int64_t row, int64_t col, float acc) {
     using E = Elem<DT>;
@@ -36,13 +51,13 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& e, int64_t row, int64_t
             static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(acc);
         } else {
             const float g = E::rnd(acc);
-            static_cast<T*>(e.out2)[row * e.ldo2 + (col - e.split)] = E::from_f(g / (1.0f + expf(-g)));
+            static_cast<T*>(e.out2)[row * e.ldo2 + (col - e.split)] = E::from_f(silu_fast(g));
         }
     } else if (KIND == EPI_SSM_PROJ) {
         if (col < e.split) {
             // dt = softplus(u W_dt^T + b_dt)  (ssm.py:330; threshold 20)
             const float v = E::rnd(acc + E::load(static_cast<const T*>(e.bias) + col));
-            const float sp = v > 20.f ? v : log1pf(expf(v));
+            const float sp = softplus_f(v);
             static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(sp);
         } else {
             static_cast<T*>(e.out2)[row * e.ldo2 + (col - e.split)] = E::from_f(acc);
@@ -115,7 +130,7 @@ __device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, i
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const float g = E::rnd(acc[j]);
-                o[j] = g / (1.0f + expf(-g));
+                o[j] = silu_fast(g);
             }
             dst = static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
         }
@@ -126,7 +141,7 @@ __device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, i
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const float v = E::rnd(acc[j] + bias[j]);
-                o[j] = v > 20.f ? v : log1pf(expf(v));
+                o[j] = softplus_f(v);
             }
             dst = static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col;
         } else {
@@ -162,6 +177,9 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
@@ -245,30 +263,47 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 }
 
 constexpr int kBM = 128, kBK = 64;
+constexpr int kEpiWarps = 8;                       // two per TMEM lane quarter
+constexpr int kTcThreads = 64 + 32 * kEpiWarps;    // TMA warp, MMA warp, epilogue warps
+constexpr int kAccStride = 256;                    // TMEM columns between the two accumulators
+constexpr uint32_t kTmemCols = 512;
 
 template <int BN, int STAGES>
 struct TcSmem {
     __nv_bfloat16 a[STAGES][kBM * kBK];
     __nv_bfloat16 b[STAGES][BN * kBK];
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
-    uint64_t acc;
+    uint64_t full[STAGES];       // TMA -> MMA: k-block landed
+    uint64_t empty[STAGES];      // MMA -> TMA: k-block consumed
+    uint64_t acc_full[2];        // MMA -> epilogue: accumulator complete
+    uint64_t acc_empty[2];       // epilogue -> MMA: accumulator drained
     uint32_t tmem_base;
 };
 
+// Deepest ring that fits next to the tile of BN columns (<= 6 stages).
+template <int BN> struct TcStages {
+    static constexpr int bytes = (kBM + BN) * kBK * 2;
+    static constexpr int value = (220 * 1024) / bytes > 6 ? 6 : (220 * 1024) / bytes;
+};
+
+// Tiles are numbered m-major in groups: tile t covers output rows
+// (t / n_tiles) * 128 and columns (t % n_tiles) * BN, so the CTAs working at
+// the same time share A row blocks through L2.
 template <int KIND, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(kTcThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                int64_t M, int64_t N, int64_t K, const int* m_count, EpiArgs epi, unsigned* err) {
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= kAccStride, "tile width");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
     auto& S = *reinterpret_cast<TcSmem<BN, STAGES>*>(base);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m0 = (int64_t)blockIdx.y * kBM, n0 = (int64_t)blockIdx.x * BN;
     const int64_t m_eff = m_count ? (int64_t)*m_count : M;
-    if (m0 >= m_eff) return;
+    const int m_tiles = (int)((m_eff + kBM - 1) / kBM);
+    const int n_tiles = (int)((N + BN - 1) / BN);
+    const int total = m_tiles * n_tiles;
     const int nk = (int)((K + kBK - 1) / kBK);
+    if ((int)blockIdx.x >= total) return;
 
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&map_a);
@@ -277,12 +312,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             mbar_init(smem_u32(&S.full[s]), 1);
             mbar_init(smem_u32(&S.empty[s]), 1);
         }
-        mbar_init(smem_u32(&S.acc), 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&S.acc_full[i]), 1);
+            mbar_init(smem_u32(&S.acc_empty[i]), kEpiWarps);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(smem_u32(&S.tmem_base)), "r"(BN));
+                     ::"r"(smem_u32(&S.tmem_base)), "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -290,53 +328,81 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     tc_fence_after();
     const uint32_t tmem = S.tmem_base;
 
-    if (warp == 0 && lane == 0) {
-        // ---------------- TMA producer ----------------
-        constexpr uint32_t bytes = (uint32_t)((kBM + BN) * kBK * sizeof(__nv_bfloat16));
-        for (int kb = 0; kb < nk; ++kb) {
-            const int s = kb % STAGES;
-            if (kb >= STAGES && !mbar_wait(smem_u32(&S.empty[s]), ((kb / STAGES) - 1) & 1)) {
-                atomicOr(err, ERRF_TIMEOUT_PRODUCER);
-                break;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            constexpr uint32_t bytes = (uint32_t)((kBM + BN) * kBK * sizeof(__nv_bfloat16));
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                const int m0 = (tile / n_tiles) * kBM, n0 = (tile % n_tiles) * BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait(smem_u32(&S.empty[s]), ((it / STAGES) - 1) & 1)) {
+                        atomicOr(err, ERRF_TIMEOUT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(smem_u32(&S.full[s]), bytes);
+                    tma_load_2d(smem_u32(S.a[s]), &map_a, smem_u32(&S.full[s]), kb * kBK, m0);
+                    tma_load_2d(smem_u32(S.b[s]), &map_b, smem_u32(&S.full[s]), kb * kBK, n0);
+                }
             }
-            mbar_expect_tx(smem_u32(&S.full[s]), bytes);
-            tma_load_2d(smem_u32(S.a[s]), &map_a, smem_u32(&S.full[s]), kb * kBK, (int)m0);
-            tma_load_2d(smem_u32(S.b[s]), &map_b, smem_u32(&S.full[s]), kb * kBK, (int)n0);
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
-        constexpr uint32_t idesc = idesc_bf16(kBM, BN);
-        for (int kb = 0; kb < nk; ++kb) {
-            const int s = kb % STAGES;
-            if (!mbar_wait(smem_u32(&S.full[s]), (kb / STAGES) & 1)) {
-                atomicOr(err, ERRF_TIMEOUT_MMA);
-                break;
-            }
-            tc_fence_after();
-            const uint32_t sa = smem_u32(S.a[s]), sb = smem_u32(S.b[s]);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+            int it = 0, local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++local) {
+                const int buf = local & 1;
+                if (local >= 2 && !mbar_wait(smem_u32(&S.acc_empty[buf]), ((local >> 1) - 1) & 1)) {
+                    atomicOr(err, ERRF_TIMEOUT_MMA);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * kAccStride);
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(smem_u32(&S.full[s]), (it / STAGES) & 1)) {
+                        atomicOr(err, ERRF_TIMEOUT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(S.a[s]), sb = smem_u32(S.b[s]);
 #pragma unroll
-            for (int k = 0; k < kBK / 16; ++k) {
-                // advance 16 bf16 (32 bytes) along K inside the swizzle atom
-                tc_mma(tmem, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), idesc,
-                       (kb | k) ? 1u : 0u);
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        // advance 16 bf16 (32 bytes) along K inside the swizzle atom
+                        tc_mma(d, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), idesc,
+                               (kb | k) ? 1u : 0u);
+                    }
+                    tc_commit(smem_u32(&S.empty[s]));
+                }
+                if (ok) tc_commit(smem_u32(&S.acc_full[buf]));
             }
-            tc_commit(smem_u32(&S.empty[s]));
         }
-        tc_commit(smem_u32(&S.acc));
-    } else if (warp >= 2) {
+    } else {
         // ---------------- epilogue: TMEM -> registers -> global ----------------
         const int q = warp & 3;                     // TMEM lane quarter this warp may access
-        const int64_t row = m0 + q * 32 + lane;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&S.acc), 0));
-        __syncwarp();                               // tcgen05.ld is .sync.aligned: whole warp, converged
-        if (!ok) {
-            if (lane == 0) atomicOr(err, ERRF_TIMEOUT_EPILOGUE);
-        } else {
+        const int half = (warp - 2) >> 2;           // which 32-column chunks: half, half + 2, ...
+        int local = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+            const int buf = local & 1;
+            const int64_t m0 = (int64_t)(tile / n_tiles) * kBM, n0 = (int64_t)(tile % n_tiles) * BN;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&S.acc_full[buf]), (local >> 1) & 1));
+            __syncwarp();                           // tcgen05.ld is .sync.aligned: whole warp, converged
+            if (!ok) {
+                if (lane == 0) atomicOr(err, ERRF_TIMEOUT_EPILOGUE);
+                break;
+            }
             tc_fence_after();
+            const int64_t row = m0 + q * 32 + lane;
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = 32 * half; c < BN; c += 64) {
                 float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kAccStride + c), v);
                 if (row < m_eff) {
 #pragma unroll
                     for (int g = 0; g < 4; ++g) {
@@ -345,6 +411,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&S.acc_empty[buf]));
         }
     }
     tc_fence_before();
@@ -352,7 +421,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
 }
 
@@ -439,8 +508,9 @@ static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols,
     return NT_OK;
 }
 
-template <int KIND, int BN, int STAGES>
+template <int KIND, int BN>
 static int launch_tc(const GemmArgs& g, cudaStream_t stream) {
+    constexpr int STAGES = TcStages<BN>::value;
     CUtensorMap ma, mb;
     int rc = make_map(&ma, g.A, g.M, g.K, g.lda, kBM);
     if (rc) return rc;
@@ -450,16 +520,39 @@ static int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     auto kern = gemm_tc_kernel<KIND, BN, STAGES>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "gemm: smem attribute: %s", cudaGetErrorString(e));
-    int dev = 0;
+    int dev = 0, sms = 148;
     cudaGetDevice(&dev);
-    dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + kBM - 1) / kBM));
-    kern<<<grid, 192, smem, stream>>>(ma, mb, g.M, g.N, g.K, g.m_count, g.epi, device_error_word(dev));
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
+    const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+    kern<<<grid, kTcThreads, smem, stream>>>(ma, mb, g.M, g.N, g.K, g.m_count, g.epi, device_error_word(dev));
     return check_launch("gemm_tc_kernel");
+}
+
+// Tile width: the candidate that wastes the fewest columns of N (ties go to
+// the wider tile, which re-reads A fewer times).
+static int pick_bn(int64_t N) {
+    static const int cand[] = {256, 224, 192, 160, 128};
+    int best = 128;
+    int64_t best_pad = -1;
+    for (int bn : cand) {
+        const int64_t pad = ((N + bn - 1) / bn) * bn - N;
+        if (best_pad < 0 || pad < best_pad) { best = bn; best_pad = pad; }
+    }
+    return best;
 }
 
 template <int KIND>
 static int launch_kind(int dtype, const GemmArgs& g, cudaStream_t stream) {
-    if (dtype == NT_BF16) return launch_tc<KIND, 128, 3>(g, stream);
+    if (dtype == NT_BF16) {
+        switch (pick_bn(g.N)) {
+            case 256: return launch_tc<KIND, 256>(g, stream);
+            case 224: return launch_tc<KIND, 224>(g, stream);
+            case 192: return launch_tc<KIND, 192>(g, stream);
+            case 160: return launch_tc<KIND, 160>(g, stream);
+            default: return launch_tc<KIND, 128>(g, stream);
+        }
+    }
     dim3 grid((unsigned)((g.N + 63) / 64), (unsigned)((g.M + 63) / 64));
     gemm_f32_kernel<KIND><<<grid, 256, 0, stream>>>(g.M, g.N, g.K, static_cast<const float*>(g.A), g.lda,
                                                      static_cast<const float*>(g.Bw), g.ldb, g.m_count, g.epi);

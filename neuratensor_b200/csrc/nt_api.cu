@@ -110,12 +110,12 @@ SparseWs sparse_ws(void* ws, int dtype, int64_t M, int64_t K) {
 
 struct BlockWs {
     void *xn, *h, *gate, *spikes, *dt, *bc, *o;
-    unsigned short* partials;
-    unsigned char* flags;
+    unsigned* row_bits;
     int *pos, *idx, *counters;
     int64_t bytes;
 };
-BlockWs block_ws(void* ws, int dtype, int64_t M, int64_t dm, int64_t di, int64_t N) {
+BlockWs block_ws(void* ws, int dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N) {
+    const int64_t M = B * T;
     Carve c(ws);
     BlockWs w;
     const int64_t es = esize(dtype);
@@ -126,8 +126,7 @@ BlockWs block_ws(void* ws, int dtype, int64_t M, int64_t dm, int64_t di, int64_t
     w.dt = c.take<char>(M * di * es);
     w.bc = c.take<char>(M * 2 * N * es);
     w.o = c.take<char>(M * di * es);
-    w.partials = c.take<unsigned short>(M * ((di + kLifChannels - 1) / kLifChannels) * 2);
-    w.flags = c.take<unsigned char>(M);
+    w.row_bits = c.take<unsigned>(4 * ((di + kLifChannels - 1) / kLifChannels) * B * ((T + 31) / 32));
     w.pos = c.take<int>(M * 4);
     w.idx = c.take<int>(M * 4);
     w.counters = c.take<int>(64);
@@ -264,7 +263,7 @@ int nt_sparse_out_proj(int dtype, int64_t M, int64_t K, int64_t Nout, const void
     GemmArgs g{};
     g.M = M; g.N = Nout; g.K = K;
     g.A = w.oc; g.lda = K; g.Bw = W; g.ldb = K; g.m_count = w.counters + 2;
-    g.epi.kind = EPI_SCATTER; g.epi.out = out; g.epi.ldo = Nout; g.epi.row_idx = w.idx;
+    g.epi.kind = EPI_SCATTER; g.epi.out = out; g.epi.ldo = Nout; g.epi.row_idx = w.idx; g.epi.row_sparse = w.counters + 1;
     NT_TRY(launch_gemm(dtype, g, st));
     return launch_fill_inactive(dtype, M, Nout, w.pos, w.counters, nullptr, out, st);
 }
@@ -302,7 +301,7 @@ int nt_rmsnorm_in_proj(int dtype, int64_t M, int64_t dm, int64_t di, const void*
 // FusedSpikeBlock.forward
 // ---------------------------------------------------------------------------
 int64_t nt_block_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N) {
-    return block_ws(nullptr, dtype, B * T, dm, di, N).bytes;
+    return block_ws(nullptr, dtype, B, T, dm, di, N).bytes;
 }
 
 int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N,
@@ -319,7 +318,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         !mem_out || !state_out || !out)
         return fail(NT_ERR_ARG, "nt_block_forward: null pointer");
     const int64_t M = B * T;
-    BlockWs w = block_ws(workspace, dtype, M, dm, di, N);
+    BlockWs w = block_ws(workspace, dtype, B, T, dm, di, N);
     if (!workspace || workspace_bytes < w.bytes)
         return fail(NT_ERR_WORKSPACE, "nt_block_forward: workspace %lld < %lld bytes", (long long)workspace_bytes,
                     (long long)w.bytes);
@@ -340,16 +339,15 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         g.epi.split = di;
         NT_TRY(launch_gemm(dtype, g, st));
     }
-    // (a) LIF -> spikes, membrane, per-row counts
-    const int64_t n_cblk = (di + kLifChannels - 1) / kLifChannels;
+    // (a) LIF -> spikes, membrane, row-activity bits
+    const int64_t n_cblk = (di + kLifChannels - 1) / kLifChannels, n_words = (T + 31) / 32;
     {
         LifArgs a{B, T, di, w.h, T * di, di, beta, threshold, mem_in, mem_out, w.spikes, T * di, di,
-                  spike_count, w.partials, n_cblk};
+                  spike_count, w.row_bits, n_words};
         NT_TRY(launch_lif_scan(dtype, dtype, a, st));
     }
-    // row activity + compaction (the density decision of _sparse_out_proj)
-    NT_TRY(launch_row_any_partials(M, n_cblk, w.partials, w.flags, st));
-    NT_TRY(launch_compact_rows(M, w.flags, w.pos, w.idx, w.counters, nullptr, sparse ? 1 : 0, st));
+    // density decision of _sparse_out_proj and, when sparse, the row compaction
+    NT_TRY(launch_compact_row_bits(B, T, n_cblk, w.row_bits, w.pos, w.idx, w.counters, sparse ? 1 : 0, st));
     // (b) dt | B | C projections of the spikes
     {
         GemmArgs g{};
@@ -372,7 +370,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         g.M = M; g.N = dm; g.K = di;
         g.A = w.o; g.lda = di; g.Bw = W_out; g.ldb = di; g.m_count = w.counters + 2;
         g.epi.kind = EPI_OUT_PROJ; g.epi.out = out; g.epi.ldo = dm; g.epi.scale = out_scale; g.epi.resid = x;
-        g.epi.ldr = dm; g.epi.row_idx = w.idx;
+        g.epi.ldr = dm; g.epi.row_idx = w.idx; g.epi.row_sparse = w.counters + 1;
         NT_TRY(launch_gemm(dtype, g, st));
     }
     // rows skipped by the sparse branch: out = 0 * out_scale + x = x

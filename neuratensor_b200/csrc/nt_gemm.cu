@@ -34,6 +34,11 @@ __device__ __forceinline__ float softplus_f(float v) {
     const float l = z < 1e-2f ? z * (1.f - z * (0.5f - z * (1.f / 3.f))) : __logf(1.f + z);
     return fmaxf(v, 0.f) + l;
 }
+// Output row of accumulator row `row` for the scattering epilogues.
+__device__ __forceinline__ int64_t out_row(const EpiArgs& e, int64_t row) {
+    const bool mapped = e.row_idx && (!e.row_sparse || *e.row_sparse != 0);
+    return mapped ? (int64_t)e.row_idx[row] : row;
+}
 // silu(g) = g * sigmoid(g)
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 template <int DT, int KIND>
@@ -64,14 +69,14 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& e, int64_t row, int64_t
         }
     } else if (KIND == EPI_OUT_PROJ) {
         // out = out_proj(o) * out_scale + residual  (fused.py:138)
-        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+        const int64_t r = out_row(e, row);
         const float s = E::load(static_cast<const T*>(e.scale));
         float v = E::rnd(acc);
         v = E::rnd(v * s);
         v = E::rnd(v + E::load(static_cast<const T*>(e.resid) + r * e.ldr + col));
         static_cast<T*>(e.out)[r * e.ldo + col] = E::from_f(v);
     } else {  // EPI_SCATTER
-        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+        const int64_t r = out_row(e, row);
         static_cast<T*>(e.out)[r * e.ldo + col] = E::from_f(acc);
     }
 }
@@ -150,7 +155,7 @@ __device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, i
             dst = static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
         }
     } else if (KIND == EPI_OUT_PROJ) {
-        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+        const int64_t r = out_row(e, row);
         const float s = E::load(static_cast<const __nv_bfloat16*>(e.scale));
         float res[8];
         unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.resid) + r * e.ldr + col)), res);
@@ -158,7 +163,7 @@ __device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, i
         for (int j = 0; j < 8; ++j) o[j] = E::rnd(E::rnd(E::rnd(acc[j]) * s) + res[j]);
         dst = static_cast<__nv_bfloat16*>(e.out) + r * e.ldo + col;
     } else {  // EPI_SCATTER
-        const int64_t r = e.row_idx ? (int64_t)e.row_idx[row] : row;
+        const int64_t r = out_row(e, row);
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = acc[j];
         dst = static_cast<__nv_bfloat16*>(e.out) + r * e.ldo + col;

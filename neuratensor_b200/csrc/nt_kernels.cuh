@@ -15,8 +15,10 @@ struct LifArgs {
     const void* mem_in; void* mem_out;
     void* spikes; int64_t s_sb, s_st;
     unsigned long long* spike_count;       // optional, += spikes
-    unsigned short* row_partials;          // optional [B*T][n_cblk] per-row counts
-    int64_t n_cblk;                        // = ceil(C / kLifChannels)
+    // optional row activity: bit (t % 32) of row_bits[(cblk * B + b) * n_words + t / 32]
+    // is set when row (b, t) has a spike among the channels of block cblk
+    unsigned* row_bits;
+    int64_t n_words;                       // = ceil(T / 32)
 };
 // math: NT_F32 (exact fp32 recurrence) or NT_BF16 (bf16 rounding after each op)
 int launch_lif_scan(int dtype, int math, const LifArgs& a, cudaStream_t stream);
@@ -53,17 +55,21 @@ int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w
 // Row activity: flags[r] = any(spikes[r, :] != 0) for a dense [M,K] matrix.
 int launch_row_any(int dtype, int64_t M, int64_t K, const void* spikes, unsigned char* flags,
                    cudaStream_t stream);
-// Row activity from LIF per-row partial counts [M][n_cblk].
-int launch_row_any_partials(int64_t M, int64_t n_cblk, const unsigned short* partials,
-                            unsigned char* flags, cudaStream_t stream);
-// Exclusive scan of flags -> row_pos (position among active rows, or -1),
-// row_idx (inverse map, first n_active entries), counters[0] = n_active,
-// counters[1] = 1 when the sparse branch is taken (2*n_active <= M).
+// Exclusive scan of flags -> counters[0] = n_active, counters[1] = 1 when the
+// sparse branch is taken (2*n_active <= M), counters[2] = rows the out_proj
+// GEMM processes.  Only on the sparse branch are row_pos (position among
+// active rows, or -1) and row_idx (inverse map, first n_active entries)
+// written; consumers treat both as the identity when counters[1] == 0.
 // n_active_out (optional) receives n_active as int64.
 int launch_compact_rows(int64_t M, const unsigned char* flags, int* row_pos, int* row_idx,
                         int* counters, long long* n_active_out, int sparse_enabled,
                         cudaStream_t stream);
-// Gather active rows of src [M,K] into dst [n_active,K] (dst row i = src row row_idx[i]).
+// The same decision and maps from the LIF's row-activity bits (M = B*T rows,
+// n_cblk channel blocks, layout of LifArgs::row_bits).
+int launch_compact_row_bits(int64_t B, int64_t T, int64_t n_cblk, const unsigned* row_bits, int* row_pos,
+                            int* row_idx, int* counters, int sparse_enabled, cudaStream_t stream);
+// Gather active rows of src [M,K] into dst [n_active,K] (dst row i = src row row_idx[i];
+// every row, in order, when counters[1] == 0).
 int launch_gather_rows(int dtype, int64_t M, int64_t K, const void* src, const int* row_idx,
                        const int* counters, void* dst, cudaStream_t stream);
 // Rows skipped by the sparse branch: dst[r,:] = fill (0) or src[r,:] (residual copy).
@@ -90,6 +96,7 @@ struct EpiArgs {
     const void* scale;         // EPI_OUT_PROJ: pointer to one dtype value
     const void* resid; int64_t ldr;
     const int* row_idx;        // row map for compacted A rows (nullptr: identity)
+    const int* row_sparse;     // when set and *row_sparse == 0, row_idx is the identity
     int vec;                   // 1: outputs, residual and bias allow 16-byte accesses per 8 columns
 };
 struct GemmArgs {

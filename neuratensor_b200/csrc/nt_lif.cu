@@ -156,12 +156,21 @@ lif_scan_kernel(LifArgs a) {
                 if (c0 + cc < a.C) sb[(t0 + tt) * a.s_st + c0 + cc] = spk_tile[tt][cc];
             }
         }
-        for (int tt = tid; tt < nt; tt += kLifChannels) {
+        // per-row spike counts; row-activity words (32 rows each) of this channel block
+        static_assert(kLifSteps <= kLifChannels && kLifSteps % 32 == 0, "one thread per tile row");
+        {
+            const int tt = tid;
             unsigned cnt = 0;
+            if (tt < nt) {
 #pragma unroll
-            for (int w = 0; w < kLifChannels / 32; ++w) cnt += __popc(row_mask[tt][w]);
+                for (int w = 0; w < kLifChannels / 32; ++w) cnt += __popc(row_mask[tt][w]);
+            }
             local_count += cnt;
-            if (a.row_partials) a.row_partials[(b * a.T + t0 + tt) * a.n_cblk + blockIdx.x] = (unsigned short)cnt;
+            if (a.row_bits && tt < kLifSteps) {
+                const unsigned word = __ballot_sync(0xffffffffu, cnt != 0);
+                const int64_t wi = t0 / 32 + tt / 32;
+                if (lane == 0 && wi < a.n_words) a.row_bits[((int64_t)blockIdx.x * a.B + b) * a.n_words + wi] = word;
+            }
         }
         __syncthreads();   // spike tile is rewritten by the next tile
     }

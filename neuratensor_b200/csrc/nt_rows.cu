@@ -94,39 +94,17 @@ int launch_row_any(int dtype, int64_t M, int64_t K, const void* spikes, unsigned
     return check_launch("row_any_kernel");
 }
 
-__global__ void __launch_bounds__(256) row_any_partials_kernel(int64_t M, int64_t n, const unsigned short* p, unsigned char* flags) {
-    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M; r += (int64_t)gridDim.x * blockDim.x) {
-        unsigned acc = 0;
-        for (int64_t j = 0; j < n; ++j) acc |= p[r * n + j];
-        flags[r] = acc ? 1 : 0;
-    }
-}
-
-int launch_row_any_partials(int64_t M, int64_t n_cblk, const unsigned short* partials, unsigned char* flags,
-                            cudaStream_t stream) {
-    const int64_t blocks = std::min<int64_t>((M + 255) / 256, 148 * 8);
-    row_any_partials_kernel<<<(unsigned)blocks, 256, 0, stream>>>(M, n_cblk, partials, flags);
-    return check_launch("row_any_partials_kernel");
-}
-
 // ---------------------------------------------------------------------------
 // Single-CTA stream compaction.  counters[0] = n_active, counters[1] = 1 when
 // the sparse branch is taken, counters[2] = rows the out_proj GEMM processes
-// (n_active when sparse, M when dense).  row_idx lists those rows; row_pos
-// maps a row to its compacted position (-1 when skipped).
+// (n_active when sparse, M when dense).  On the sparse branch row_idx lists
+// those rows and row_pos maps a row to its compacted position (-1 when
+// skipped); on the dense branch both stay unwritten and mean the identity.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) compact_rows_kernel(int64_t M, const unsigned char* flags, int* row_pos,
-                                                            int* row_idx, int* counters, long long* n_active_out,
-                                                            int sparse_enabled) {
-    __shared__ int warp_tot[32];
-    __shared__ int s_total;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t per = (M + 1023) / 1024;
-    const int64_t r0 = tid * per, r1 = (r0 + per < M) ? r0 + per : M;
-    int cnt = 0;
-    for (int64_t r = r0; r < r1; ++r) cnt += flags[r] ? 1 : 0;
-    // inclusive scan of cnt across the CTA
-    int v = cnt;
+
+// Inclusive scan of one int per thread across a 1024-thread CTA; *total gets the sum.
+__device__ __forceinline__ int cta_scan_1024(int v, int* warp_tot, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
         const int o = __shfl_up_sync(0xffffffffu, v, off);
@@ -141,20 +119,31 @@ __global__ void __launch_bounds__(1024) compact_rows_kernel(int64_t M, const uns
             const int o = __shfl_up_sync(0xffffffffu, w, off);
             if (lane >= off) w += o;
         }
-        warp_tot[lane] = w;            // inclusive
-        if (lane == 31) s_total = w;
+        warp_tot[lane] = w;
+        if (lane == 31) *total = w;
     }
     __syncthreads();
+    return v + (warp ? warp_tot[warp - 1] : 0);
+}
+__global__ void __launch_bounds__(1024) compact_rows_kernel(int64_t M, const unsigned char* flags, int* row_pos,
+                                                            int* row_idx, int* counters, long long* n_active_out,
+                                                            int sparse_enabled) {
+    __shared__ int warp_tot[32];
+    __shared__ int s_total;
+    const int tid = threadIdx.x;
+    const int64_t per = (M + 1023) / 1024;
+    const int64_t r0 = tid * per, r1 = (r0 + per < M) ? r0 + per : M;
+    int cnt = 0;
+    for (int64_t r = r0; r < r1; ++r) cnt += flags[r] ? 1 : 0;
+    const int incl = cta_scan_1024(cnt, warp_tot, &s_total);
     const int n_active = s_total;
     const bool sparse = sparse_enabled && (2LL * n_active <= M);
-    int pos = v - cnt + (warp ? warp_tot[warp - 1] : 0);   // exclusive prefix
+    int pos = incl - cnt;                                  // exclusive prefix
     if (sparse) {
         for (int64_t r = r0; r < r1; ++r) {
             if (flags[r]) { row_pos[r] = pos; row_idx[pos] = (int)r; ++pos; }
             else row_pos[r] = -1;
         }
-    } else {
-        for (int64_t r = r0; r < r1; ++r) { row_pos[r] = (int)r; row_idx[r] = (int)r; }
     }
     if (tid == 0) {
         counters[0] = n_active;
@@ -171,15 +160,68 @@ int launch_compact_rows(int64_t M, const unsigned char* flags, int* row_pos, int
     return check_launch("compact_rows_kernel");
 }
 
+// The same from row-activity words: word (b, w) covers rows b*T + 32w + j,
+// j < min(32, T - 32w); a row is active when any channel block set its bit.
+// Thread i owns a run of consecutive words.
+__global__ void __launch_bounds__(1024) compact_row_bits_kernel(int64_t B, int64_t T, int64_t n_cblk,
+                                                                const unsigned* bits, int* row_pos, int* row_idx,
+                                                                int* counters, int sparse_enabled) {
+    __shared__ int warp_tot[32];
+    __shared__ int s_total;
+    const int64_t n_words = (T + 31) / 32, words = B * n_words;
+    const int64_t per = (words + 1023) / 1024;
+    const int64_t w0 = threadIdx.x * per, w1 = (w0 + per < words) ? w0 + per : words;
+    auto word_mask = [&](int64_t g) -> unsigned {
+        const int64_t b = g / n_words, w = g % n_words;
+        unsigned m = 0;
+        for (int64_t k = 0; k < n_cblk; ++k) m |= bits[(k * B + b) * n_words + w];
+        const int64_t valid = T - 32 * w;
+        return valid >= 32 ? m : (m & ((1u << valid) - 1u));
+    };
+    int cnt = 0;
+    for (int64_t g = w0; g < w1; ++g) cnt += __popc(word_mask(g));
+    const int incl = cta_scan_1024(cnt, warp_tot, &s_total);
+    const int64_t M = B * T;
+    const int n_active = s_total;
+    const bool sparse = sparse_enabled && (2LL * n_active <= M);
+    if (sparse) {
+        int pos = incl - cnt;
+        for (int64_t g = w0; g < w1; ++g) {
+            const unsigned m = word_mask(g);
+            const int64_t b = g / n_words, w = g % n_words;
+            const int64_t valid = T - 32 * w < 32 ? T - 32 * w : 32;
+            for (int j = 0; j < valid; ++j) {
+                const int64_t r = b * T + 32 * w + j;
+                if ((m >> j) & 1u) { row_pos[r] = pos; row_idx[pos] = (int)r; ++pos; }
+                else row_pos[r] = -1;
+            }
+        }
+    }
+    if (threadIdx.x == 0) {
+        counters[0] = n_active;
+        counters[1] = sparse ? 1 : 0;
+        counters[2] = sparse ? n_active : (int)M;
+    }
+}
+
+int launch_compact_row_bits(int64_t B, int64_t T, int64_t n_cblk, const unsigned* row_bits, int* row_pos,
+                            int* row_idx, int* counters, int sparse_enabled, cudaStream_t stream) {
+    if (B * T > (int64_t)INT32_MAX) return fail(NT_ERR_ARG, "compact_row_bits: B*T too large");
+    compact_row_bits_kernel<<<1, 1024, 0, stream>>>(B, T, n_cblk, row_bits, row_pos, row_idx, counters,
+                                                    sparse_enabled);
+    return check_launch("compact_row_bits_kernel");
+}
+
 // dst[i, :] = src[row_idx[i], :] for i < counters[2].  Rows of 16-byte chunks.
 __global__ void __launch_bounds__(256) gather_rows_kernel(int64_t M, int64_t row_bytes, const char* src,
                                                           const int* row_idx, const int* counters, char* dst) {
     const int64_t m = counters[2];
+    const bool mapped = counters[1] != 0;
     const int64_t chunks = row_bytes / 16;
     const int64_t total = m * chunks;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / chunks, k = i % chunks;
-        const int64_t sr = row_idx[r];
+        const int64_t sr = mapped ? row_idx[r] : r;
         reinterpret_cast<uint4*>(dst + r * row_bytes)[k] = __ldg(reinterpret_cast<const uint4*>(src + sr * row_bytes) + k);
     }
 }

@@ -221,8 +221,8 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     from neuratensor_b200 import InferenceEngine, NeuraTensorModel, get_preset
-    from neuratensor_b200.native import load
-    load()
+    from neuratensor_b200 import native
+    native.load()
     torch.manual_seed(SEED)
     model = NeuraTensorModel(get_preset(PRESET))
     eng = InferenceEngine(model, device=f"cuda:{local}", dtype=torch.bfloat16)
@@ -247,6 +247,7 @@ def run_ours(args):
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
         counts = None
+        launches0 = native.launch_count()
         with Clocks(local) as clk:
             torch.cuda.synchronize(dev)
             for i, (a, b) in enumerate(evs):
@@ -255,6 +256,7 @@ def run_ours(args):
                 counts = step(i)
                 b.record(stream)
             torch.cuda.synchronize(dev)
+        launches = native.launch_count() - launches0
         if world > 1:
             dist.barrier()
         ms = sum(a.elapsed_time(b) for a, b in evs)
@@ -305,7 +307,6 @@ def run_ours(args):
     tokens = BATCH * SEQ * world * args.steps
     value = tokens / (ms / 1000.0)
     e2e_value = tokens / (e2e_ms / 1000.0)
-    launches_per_step = 9 * model.config.n_layers
     cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
     line = {
         "metric": "tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -316,7 +317,7 @@ def run_ours(args):
                    "l2": "flushed (256 MiB write) before every timed step"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * SEQ * 8,
                 "d2h_bytes_per_step": 8 * model.config.n_layers},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches,
         "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
         "spike_rate": metrics["spike_rate"],
     }

@@ -69,6 +69,10 @@ NT_API int nt_device_supported(int device);
  * a bounded wait expires.  Synchronises the device.  *flags == 0 means no
  * kernel reported an error. */
 NT_API int nt_get_error_flag(int device, unsigned* flags, int clear);
+/* Kernels this library has launched in this process (all devices, all host
+ * threads).  Reading it before and after a call counts that call's launches.
+ * No counterpart in the reference, which launches no kernels of its own. */
+NT_API unsigned long long nt_launch_count(void);
 
 /* (a) LIF membrane recurrence -- LIFLayer.forward (snn.py:264-312).
  * Per channel c and step t:  V = beta[c]*V + x[t,c]  (a product then a sum,

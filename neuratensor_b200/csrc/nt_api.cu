@@ -3,6 +3,7 @@
 // point replaces are in include/neuratensor_native.h.
 #include "nt_kernels.cuh"
 
+#include <atomic>
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
@@ -29,7 +30,12 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
+// Every launcher calls check_launch right after its launch, so this counts
+// the library's kernel launches.
+std::atomic<unsigned long long> g_launches{0};
+
 int check_launch(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
     return NT_OK;
@@ -156,6 +162,8 @@ int nt_device_supported(int device) {
         return fail(NT_ERR_ARCH, "device %d is sm_%d%d; this library is built for sm_100a", device, p.major, p.minor);
     return NT_OK;
 }
+
+unsigned long long nt_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int nt_get_error_flag(int device, unsigned* flags, int clear) {
     if (!flags) return fail(NT_ERR_ARG, "nt_get_error_flag: flags is NULL");

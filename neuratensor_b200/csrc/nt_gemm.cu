@@ -104,12 +104,30 @@ __device__ __forceinline__ void unpack_bf16x8(uint4 q, float (&o)[8]) {
     }
 }
 
+// Eight consecutive columns [col, col+8) of one row, in two phases so the
+// epilogue can issue its global reads (bias, residual) before it waits for
+// the accumulator: epi_pre8 loads them, epi_fin8 applies the epilogue and
+// stores.  Vector path: the eight outputs leave as one 16-byte store when the
+// host marked the layout 16-byte compatible (e.vec) and the group lies inside
+// [0, N) on one side of `split`; scalar fallback otherwise.  `orow` is the
+// output (and residual) row of accumulator row `row` (out_row()).
+__device__ __forceinline__ bool epi_vec8(const EpiArgs& e, int64_t col, int64_t N) { return e.vec && col + 8 <= N; }
+
 template <int KIND>
-__device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, int64_t col, int64_t N,
-                                                const float (&acc)[8]) {
+__device__ __forceinline__ uint4 epi_pre8(const EpiArgs& e, int64_t orow, int64_t col, int64_t N) {
+    if (!epi_vec8(e, col, N)) return make_uint4(0, 0, 0, 0);
+    if (KIND == EPI_SSM_PROJ && col < e.split)
+        return __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.bias) + col));
+    if (KIND == EPI_OUT_PROJ)
+        return __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.resid) + orow * e.ldr + col));
+    return make_uint4(0, 0, 0, 0);
+}
+
+template <int KIND>
+__device__ __forceinline__ void epi_fin8(const EpiArgs& e, int64_t row, int64_t orow, int64_t col, int64_t N,
+                                         const float (&acc)[8], uint4 pre) {
     using E = Elem<NT_BF16>;
-    const bool full = e.vec && (col + 8 <= N);
-    if (!full) {
+    if (!epi_vec8(e, col, N)) {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
             if (col + j < N) epi_apply<NT_BF16, KIND>(e, row, col + j, acc[j]);
@@ -133,21 +151,15 @@ __device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, i
             dst = static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col;
         } else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float g = E::rnd(acc[j]);
-                o[j] = silu_fast(g);
-            }
+            for (int j = 0; j < 8; ++j) o[j] = silu_fast(E::rnd(acc[j]));
             dst = static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
         }
     } else if (KIND == EPI_SSM_PROJ) {
         if (col < e.split) {
             float bias[8];
-            unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.bias) + col)), bias);
+            unpack_bf16x8(pre, bias);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float v = E::rnd(acc[j] + bias[j]);
-                o[j] = softplus_f(v);
-            }
+            for (int j = 0; j < 8; ++j) o[j] = softplus_f(E::rnd(acc[j] + bias[j]));
             dst = static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col;
         } else {
 #pragma unroll
@@ -155,18 +167,16 @@ __device__ __forceinline__ void epi_apply8_bf16(const EpiArgs& e, int64_t row, i
             dst = static_cast<__nv_bfloat16*>(e.out2) + row * e.ldo2 + (col - e.split);
         }
     } else if (KIND == EPI_OUT_PROJ) {
-        const int64_t r = out_row(e, row);
         const float s = E::load(static_cast<const __nv_bfloat16*>(e.scale));
         float res[8];
-        unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.resid) + r * e.ldr + col)), res);
+        unpack_bf16x8(pre, res);
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = E::rnd(E::rnd(E::rnd(acc[j]) * s) + res[j]);
-        dst = static_cast<__nv_bfloat16*>(e.out) + r * e.ldo + col;
+        dst = static_cast<__nv_bfloat16*>(e.out) + orow * e.ldo + col;
     } else {  // EPI_SCATTER
-        const int64_t r = out_row(e, row);
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = acc[j];
-        dst = static_cast<__nv_bfloat16*>(e.out) + r * e.ldo + col;
+        dst = static_cast<__nv_bfloat16*>(e.out) + orow * e.ldo + col;
     }
     *reinterpret_cast<uint4*>(dst) = pack_bf16x8(o);
 }
@@ -230,20 +240,18 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum) : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// 32 lanes x 16 columns of fp32 accumulator: thread i gets lane (row) i.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
@@ -268,7 +276,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 }
 
 constexpr int kBM = 128, kBK = 64;
-constexpr int kEpiWarps = 8;                       // two per TMEM lane quarter
+constexpr int kEpiWarps = 16;                      // four per TMEM lane quarter
 constexpr int kTcThreads = 64 + 32 * kEpiWarps;    // TMA warp, MMA warp, epilogue warps
 constexpr int kAccStride = 256;                    // TMEM columns between the two accumulators
 constexpr uint32_t kTmemCols = 512;
@@ -297,7 +305,7 @@ template <int KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                int64_t M, int64_t N, int64_t K, const int* m_count, EpiArgs epi, unsigned* err) {
-    static_assert(BN % 32 == 0 && BN >= 32 && BN <= kAccStride, "tile width");
+    static_assert(BN % 16 == 0 && BN >= 32 && BN <= kAccStride, "tile width");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
@@ -390,8 +398,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
     } else {
         // ---------------- epilogue: TMEM -> registers -> global ----------------
+        constexpr int kParts = kEpiWarps / 4;      // warps sharing a lane quarter
         const int q = warp & 3;                     // TMEM lane quarter this warp may access
-        const int half = (warp - 2) >> 2;           // which 32-column chunks: half, half + 2, ...
+        const int part = (warp - 2) >> 2;           // its 16-column chunks: part, part + kParts, ...
         int local = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
             const int buf = local & 1;
@@ -404,15 +413,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             tc_fence_after();
             const int64_t row = m0 + q * 32 + lane;
+            const bool row_ok = row < m_eff;
+            const int64_t orow = (KIND == EPI_OUT_PROJ || KIND == EPI_SCATTER) && row_ok ? out_row(epi, row) : row;
 #pragma unroll 1
-            for (int c = 32 * half; c < BN; c += 64) {
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kAccStride + c), v);
-                if (row < m_eff) {
+            for (int c = 16 * part; c < BN; c += 16 * kParts) {
+                // global reads first, so they are in flight while the accumulator is read
+                uint4 pre[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                if (row_ok) {
+                    pre[0] = epi_pre8<KIND>(epi, orow, n0 + c, N);
+                    pre[1] = epi_pre8<KIND>(epi, orow, n0 + c + 8, N);
+                }
+                float v[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kAccStride + c), v);
+                if (row_ok) {
 #pragma unroll
-                    for (int g = 0; g < 4; ++g) {
+                    for (int g = 0; g < 2; ++g) {
                         const float (&v8)[8] = *reinterpret_cast<const float(*)[8]>(v + 8 * g);
-                        epi_apply8_bf16<KIND>(epi, row, n0 + c + 8 * g, N, v8);
+                        epi_fin8<KIND>(epi, row, orow, n0 + c + 8 * g, N, v8, pre[g]);
                     }
                 }
             }

@@ -40,6 +40,7 @@ _SIGS = {
     "nt_last_error": ([], ctypes.c_char_p),
     "nt_device_supported": ([_I32], _I32),
     "nt_get_error_flag": ([_I32, ctypes.POINTER(ctypes.c_uint), _I32], _I32),
+    "nt_launch_count": ([], ctypes.c_ulonglong),
     "nt_lif_scan": ([_I32, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P], _I32),
     "nt_selective_scan": ([_I32, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I32),
     "nt_ssm_workspace_bytes": ([_I32, _I64, _I64, _I64, _I64], _I64),
@@ -325,6 +326,11 @@ def lif_ssm_fused(x: Tensor, delta: Tensor, Bm: Tensor, Cm: Tensor, log_A: Tenso
                                  sd, _p(spike_count), _stream(dev))
     _check("nt_lif_ssm_fused", rc)
     return y, spikes, mem_out, st_out
+
+
+def launch_count() -> int:
+    """Kernels this library has launched in this process (nt_launch_count)."""
+    return int(load().nt_launch_count())
 
 
 def device_error_flags(device: int = 0, clear: bool = True) -> int:

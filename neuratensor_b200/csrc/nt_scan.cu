@@ -102,27 +102,32 @@ struct ScanSmem {
     static constexpr int NP = NPT * TPC;                // padded d_state
     static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;       // elements of T per staging buffer
     static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
-    // partial-sum row pitch: 128 slots, plus CPB when a warp's reduction loads
-    // span several steps (their rows then start in different banks)
-    static constexpr int YS = 128 + (CPB < 32 ? CPB : 0);
     static constexpr int WORK_FLOATS =
-        2 * TCH * CPB + 2 * TCH * NP + TCH * YS + (MODE == 1 ? TCH * CPB : 0) + CPB + NP + TCH;
+        2 * TCH * CPB + 2 * TCH * NP + TCH * 128 + (MODE == 1 ? TCH * CPB : 0) + CPB + NP + TCH;
     static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + sizeof(float) * (size_t)WORK_FLOATS;
 };
 
-// Slot of the partial C.h sum of (sub s, channel c) within a step's row of
-// the partial-sum buffer (row pitch ScanSmem::YS).  Sub s owns CPB slots and
-// channel c sits at c ^ X(s): the 32 stores of a warp (32/TPC channels x TPC
-// subs, one step) fall in 32 distinct banks, and so do the reduction's loads
-// (consecutive channels of 32/CPB consecutive steps, one sub), whose rows the
-// pitch YS = 128 + CPB shifts by CPB banks each.
+// Partial C.h sums: one row of 128 floats per step, channel c's TPC partials
+// contiguous at c*TPC so the reduction reads them as TPC/4 float4s.  Within a
+// channel the float4 groups are XOR-swizzled by yp_x(i), i = step*CPB + c, so
+// the eight threads of a quarter-warp reading group h land in eight distinct
+// bank groups; a warp's per-step stores stay a permutation of 32 consecutive
+// floats.  (The sum does not depend on the order of a channel's groups.)
 template <int TPC>
-__device__ __forceinline__ int yp_slot(int s, int c) {
+__device__ __forceinline__ int yp_x(int i) {
+    constexpr int G = TPC / 4;                       // float4 groups per channel
+    if constexpr (G < 2) return 0;
+    else {
+        constexpr int lg = G == 2 ? 1 : G == 4 ? 2 : 3;
+        return (i >> (3 - lg)) & (G - 1);
+    }
+}
+// Slot of the partial of (step tt, channel cl, sub) in its step's row.
+template <int TPC>
+__device__ __forceinline__ int yp_slot(int tt, int cl, int sub) {
     constexpr int CPB = 128 / TPC;
-    int x = 0;
-    if constexpr (TPC == 2) x = 16 * s;
-    else if constexpr (TPC >= 4) x = (32 / TPC) * (s / (TPC / 4));
-    return s * CPB + (c ^ x);
+    if constexpr (TPC < 4) return cl * TPC + sub;
+    else return cl * TPC + 4 * ((sub >> 2) ^ yp_x<TPC>(tt * CPB + cl)) + (sub & 3);
 }
 
 // Position of state n within a staged B or C row.  Rows of 64 or more states
@@ -169,12 +174,11 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     using L = ScanSmem<TPC, NPT, T, MODE>;
     constexpr int CPB = L::CPB, NP = L::NP, kTch = L::TCH, NPR = NPT / 2;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float* w_u = reinterpret_cast<float*>(smem_raw + 2 * L::RAW_BYTES);  // [kTch][CPB] u (or x)
-    float* w_dt = w_u + kTch * CPB;                                      // [kTch][CPB]
-    float* w_B = w_dt + kTch * CPB;                                      // [kTch][NP]  B (or B/(n+1))
+    float2* w_ud = reinterpret_cast<float2*>(smem_raw + 2 * L::RAW_BYTES);  // [kTch][CPB] (u or x, dt)
+    float* w_B = reinterpret_cast<float*>(w_ud + kTch * CPB);            // [kTch][NP]  B (or B/(n+1))
     float* w_C = w_B + kTch * NP;                                        // [kTch][NP]
-    float* w_yp = w_C + kTch * NP;                                       // [kTch][YS] partial C.h (yp_slot)
-    float* w_s = w_yp + kTch * L::YS;                                    // [kTch][CPB] spikes (MODE 1 only)
+    float* w_yp = w_C + kTch * NP;                                       // [kTch][128] partial C.h (yp_slot)
+    float* w_s = w_yp + kTch * 128;                                      // [kTch][CPB] spikes (MODE 1 only)
     float* w_D = w_s + (MODE == 1 ? kTch * CPB : 0);                     // [CPB] skip weights D
     float* w_rn = w_D + CPB;                                             // [NP] 1/(n+1)
     int* w_pos = reinterpret_cast<int*>(w_rn + NP);                      // [kTch] compacted row positions
@@ -306,19 +310,20 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             Bf[4 * q] = bq.x; Bf[4 * q + 1] = bq.y; Bf[4 * q + 2] = bq.z; Bf[4 * q + 3] = bq.w;
             Cf[4 * q] = cq.x; Cf[4 * q + 1] = cq.y; Cf[4 * q + 2] = cq.z; Cf[4 * q + 3] = cq.w;
         }
+        const float2 ud = w_ud[tt * CPB + cl];
         float u;
         if (MODE == 0) {
-            u = w_u[tt * CPB + cl];
+            u = ud.x;
         } else {
             // LIF step (snn.py:177-181) in fp32, identical in every thread of the channel
-            const float m1 = __fadd_rn(__fmul_rn(beta, mem), w_u[tt * CPB + cl]);
+            const float m1 = __fadd_rn(__fmul_rn(beta, mem), ud.x);
             const float s1 = (m1 >= th) ? 1.f : 0.f;
             const float m2 = __fsub_rn(m1, __fmul_rn(th, s1));
             const bool in_seq = tt < nt;
             u = in_seq ? s1 : 0.f;
             mem = in_seq ? m2 : mem;
         }
-        const float dtv = w_dt[tt * CPB + cl];
+        const float dtv = ud.y;
         float2 av[NPR], hv[NPR];
 #pragma unroll
         for (int j = 0; j < NPR; ++j) hv[j] = make_float2(h[2 * j], h[2 * j + 1]);
@@ -356,14 +361,11 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         }
 #pragma unroll
         for (int j = 0; j < NPR; ++j) { h[2 * j] = hv[j].x; h[2 * j + 1] = hv[j].y; }
-        float2 y0 = __fmul2_rn(make_float2(Cf[0], Cf[1]), hv[0]);
-        float2 y1 = __fmul2_rn(make_float2(Cf[2], Cf[3]), hv[1]);
+        // C.h as one packed fma chain, then one add of the two lanes
+        float2 y2 = __fmul2_rn(make_float2(Cf[0], Cf[1]), hv[0]);
 #pragma unroll
-        for (int j = 2; j < NPR; j += 2) {
-            y0 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y0);
-            y1 = __ffma2_rn(make_float2(Cf[2 * j + 2], Cf[2 * j + 3]), hv[j + 1], y1);
-        }
-        yp_out = (y0.x + y0.y) + (y1.x + y1.y);
+        for (int j = 1; j < NPR; ++j) y2 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y2);
+        yp_out = y2.x + y2.y;
         u_out = u;
     };
 
@@ -381,13 +383,12 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         // ---- widen the chunk to float32 (B pre-divided by n+1 on the HiPPO path)
         const T* rb = raw_buf(kc);
         for (int i = tid * EPV; i < kTch * CPB; i += 128 * EPV) {
-            float v[EPV];
-            widen16(rb + i, v);
+            float uv[EPV], dv[EPV];
+            widen16(rb + i, uv);
+            widen16(rb + kTch * CPB + i, dv);
 #pragma unroll
-            for (int k = 0; k < EPV; k += 4) *reinterpret_cast<float4*>(w_u + i + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
-            widen16(rb + kTch * CPB + i, v);
-#pragma unroll
-            for (int k = 0; k < EPV; k += 4) *reinterpret_cast<float4*>(w_dt + i + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+            for (int k = 0; k < EPV; k += 2)
+                *reinterpret_cast<float4*>(w_ud + i + k) = make_float4(uv[k], dv[k], uv[k + 1], dv[k + 1]);
         }
         for (int i = tid * EPV; i < kTch * NP; i += 128 * EPV) {
             float bv[EPV], cv[EPV];
@@ -398,7 +399,10 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                 const int tt = (i + k) / NP, n = (i + k) % NP;     // four states of one row
                 const int o = tt * NP + bc_swz<NP>(n);
                 float4 b4 = make_float4(bv[k], bv[k + 1], bv[k + 2], bv[k + 3]);
-                if (hippo) { b4.x *= w_rn[n]; b4.y *= w_rn[n + 1]; b4.z *= w_rn[n + 2]; b4.w *= w_rn[n + 3]; }
+                if (hippo) {
+                    const float4 r4 = *reinterpret_cast<const float4*>(w_rn + n);
+                    b4.x *= r4.x; b4.y *= r4.y; b4.z *= r4.z; b4.w *= r4.w;
+                }
                 *reinterpret_cast<float4*>(w_B + o) = b4;
                 *reinterpret_cast<float4*>(w_C + o) = make_float4(cv[k], cv[k + 1], cv[k + 2], cv[k + 3]);
             }
@@ -416,7 +420,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             else static_for<0, kRun>([&](auto j) { constexpr int q = decltype(j)::value; step(r0 + q, nt, std::false_type{}, ypr[q], upr[q]); });
 #pragma unroll
             for (int q = 0; q < kRun; ++q) {
-                w_yp[(r0 + q) * L::YS + yp_slot<TPC>(sub, cl)] = ypr[q];
+                w_yp[(r0 + q) * 128 + yp_slot<TPC>(r0 + q, cl, sub)] = ypr[q];
                 if (MODE == 1) w_s[(r0 + q) * CPB + cl] = upr[q];   // every thread of the channel stores the same value
             }
         });
@@ -430,10 +434,28 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             const int tt = tid / CPB + k * TPC, cc = tid % CPB;
             const int64_t t = t0 + tt, cg = c0 + cc;
             if (tt >= nt || cg >= d) continue;
-            float yp = 0.f;
+            float yp;
+            const float* yrow = w_yp + tt * 128 + cc * TPC;
+            if constexpr (TPC == 1) {
+                yp = yrow[0];
+            } else if constexpr (TPC == 2) {
+                const float2 p = *reinterpret_cast<const float2*>(yrow);
+                yp = p.x + p.y;
+            } else {
+                // TPC/4 float4 groups (swizzled order), summed as packed pairs
+                const int x = yp_x<TPC>(i);
+                const float4 p0 = *reinterpret_cast<const float4*>(yrow + 4 * x);
+                float2 s0 = make_float2(p0.x, p0.y), s1 = make_float2(p0.z, p0.w);
 #pragma unroll
-            for (int s2 = 0; s2 < TPC; ++s2) yp += w_yp[tt * L::YS + yp_slot<TPC>(s2, cc)];
-            const float uu = MODE == 0 ? w_u[i] : w_s[i];
+                for (int g = 1; g < TPC / 4; ++g) {
+                    const float4 p = *reinterpret_cast<const float4*>(yrow + 4 * (g ^ x));
+                    s0 = __fadd2_rn(s0, make_float2(p.x, p.y));
+                    s1 = __fadd2_rn(s1, make_float2(p.z, p.w));
+                }
+                s0 = __fadd2_rn(s0, s1);
+                yp = s0.x + s0.y;
+            }
+            const float uu = MODE == 0 ? w_ud[i].x : w_s[i];
             const float yv = __fadd_rn(yp, __fmul_rn(w_D[cc], uu));
             int64_t row = row0 + t;
             if (MODE == 0) {
@@ -500,6 +522,9 @@ int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     return check_launch("ssm_scan_kernel");
 }
 
+#ifndef NT_SCAN_NARROW_CTAS
+#define NT_SCAN_NARROW_CTAS 4
+#endif
 // States per thread: 8, or 4 when 8 would leave the GPU with fewer than four
 // 128-thread CTAs per SM (the recurrence is latency-bound, so warps matter
 // more than the extra per-thread work of a narrower state slice).
@@ -511,7 +536,7 @@ int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tpc8 = pow2_at_least((N + 7) / 8);
     const int64_t ctas8 = B * ((d + 128 / tpc8 - 1) / (128 / tpc8));
-    const bool narrow = N >= 8 && tpc8 <= 16 && ctas8 < 4LL * sms;
+    const bool narrow = N >= 8 && tpc8 <= 16 && ctas8 < (int64_t)NT_SCAN_NARROW_CTAS * sms;
     if (narrow) {
         switch (pow2_at_least((N + 3) / 4)) {
             case 2: return launch_tpc<DT, SDT, MODE, 2, 4>(a, f, stream);

@@ -23,9 +23,9 @@ namespace nt {
 
 namespace {
 
-constexpr int kLifStages = 4;
-// steps per tile: 32 KB of staging for the whole ring in either dtype
-template <typename T> struct LifSteps { static constexpr int value = 128 / (int)sizeof(T); };
+constexpr int kLifStages = 3;
+// steps per tile: 256 bytes of input per channel (128 bf16 or 64 fp32 steps)
+template <typename T> struct LifSteps { static constexpr int value = 256 / (int)sizeof(T); };
 
 __device__ __forceinline__ void cp16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
@@ -71,6 +71,20 @@ template <> __device__ __forceinline__ __nv_bfloat16 spike_val<__nv_bfloat16>(bo
     return __ushort_as_bfloat16(s ? (unsigned short)0x3F80 : (unsigned short)0);
 }
 
+// Shared-memory layout of one CTA: a kLifStages-deep ring of input tiles,
+// one spike tile.
+template <typename T> struct LifSmem {
+    static constexpr int kSteps = LifSteps<T>::value;
+    static constexpr size_t tile_bytes = (size_t)kSteps * kLifChannels * sizeof(T);
+    static constexpr size_t bytes = (kLifStages + 1) * tile_bytes;
+};
+
+// Spikes in one 32-bit word of the spike tile: bit 7 of a bf16 1.0 (0x3F80)
+// or bit 23 of a float 1.0 (0x3F800000); a 0 spike is all zero bits.
+template <typename T> __device__ __forceinline__ int spikes_in_word(uint32_t w);
+template <> __device__ __forceinline__ int spikes_in_word<__nv_bfloat16>(uint32_t w) { return __popc(w & 0x00800080u); }
+template <> __device__ __forceinline__ int spikes_in_word<float>(uint32_t w) { return (w >> 23) & 1u; }
+
 template <int DT, int MATH>
 __global__ void __launch_bounds__(kLifChannels)
 lif_scan_kernel(LifArgs a) {
@@ -78,13 +92,14 @@ lif_scan_kernel(LifArgs a) {
     using T = typename E::T;
     using S = typename Elem<MATH>::T;       // state / arithmetic type
     using M = MathOf<S>;
+    using L = LifSmem<T>;
     constexpr int EPV = 16 / (int)sizeof(T);
-    constexpr int kLifSteps = LifSteps<T>::value;
-    __shared__ __align__(16) T tile[kLifStages][kLifSteps][kLifChannels];
-    __shared__ __align__(16) T spk_tile[kLifSteps][kLifChannels];
-    __shared__ unsigned row_mask[kLifSteps][kLifChannels / 32];
+    constexpr int kSteps = L::kSteps;
+    extern __shared__ __align__(16) unsigned char lif_smem[];
+    T (*tile)[kSteps][kLifChannels] = reinterpret_cast<T (*)[kSteps][kLifChannels]>(lif_smem);
+    T (*spk_tile)[kLifChannels] = reinterpret_cast<T (*)[kLifChannels]>(lif_smem + kLifStages * L::tile_bytes);
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
     const int64_t c0 = (int64_t)blockIdx.x * kLifChannels, c = c0 + tid, b = blockIdx.y;
     const bool live = c < a.C;
     const T* xb = static_cast<const T*>(a.x) + b * a.x_sb;
@@ -102,21 +117,21 @@ lif_scan_kernel(LifArgs a) {
                         ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
     const bool vec_out = full_cols && (a.s_st % EPV == 0) && (a.s_sb % EPV == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.spikes) & 15) == 0);
-    const int ntiles = (int)((a.T + kLifSteps - 1) / kLifSteps);
+    const int ntiles = (int)((a.T + kSteps - 1) / kSteps);
     constexpr int VPR = kLifChannels / EPV;      // 16-byte vectors per tile row
 
     auto issue = [&](int k) {
         if (k < ntiles) {
             T* dst = &tile[k % kLifStages][0][0];
-            const int64_t t0 = (int64_t)k * kLifSteps;
+            const int64_t t0 = (int64_t)k * kSteps;
             if (vec_in) {
-                for (int i = tid; i < kLifSteps * VPR; i += kLifChannels) {
+                for (int i = tid; i < kSteps * VPR; i += kLifChannels) {
                     const int tt = i / VPR, vv = i % VPR;
                     const int64_t t = t0 + tt;
                     if (t < a.T) cp16(dst + tt * kLifChannels + vv * EPV, xb + t * a.x_st + c0 + vv * EPV);
                 }
             } else {
-                for (int i = tid; i < kLifSteps * kLifChannels; i += kLifChannels) {
+                for (int i = tid; i < kSteps * kLifChannels; i += kLifChannels) {
                     const int tt = i / kLifChannels, cc = i % kLifChannels;
                     const int64_t t = t0 + tt;
                     dst[i] = (t < a.T && c0 + cc < a.C) ? xb[t * a.x_st + c0 + cc] : T(0.f);
@@ -133,17 +148,41 @@ lif_scan_kernel(LifArgs a) {
         wait_stages();
         __syncthreads();
         const T* xt = &tile[k % kLifStages][0][0];
-        const int64_t t0 = (int64_t)k * kLifSteps;
-        const int nt = (a.T - t0 < kLifSteps) ? (int)(a.T - t0) : kLifSteps;
-#pragma unroll 8
-        for (int tt = 0; tt < nt; ++tt) {
-            const bool fired = lif_step(v, beta, th, M::in(xt[tt * kLifChannels + tid])) && live;
-            spk_tile[tt][tid] = spike_val<T>(fired);
-            const unsigned m = __ballot_sync(0xffffffffu, fired);
-            if (lane == 0) row_mask[tt][warp] = m;
+        const int64_t t0 = (int64_t)k * kSteps;
+        const int nt = (a.T - t0 < kSteps) ? (int)(a.T - t0) : kSteps;
+        // The serial chain: one membrane update and one spike store per step.
+        // Inputs are read eight steps ahead into registers, so no shared-memory
+        // load latency sits on the chain (in program order the loads of group
+        // g+1 precede the spike stores of group g).
+        if (nt == kSteps) {
+            constexpr int G = 8;
+            T xn[G];
+#pragma unroll
+            for (int j = 0; j < G; ++j) xn[j] = xt[j * kLifChannels + tid];
+#pragma unroll 1
+            for (int g = 0; g < kSteps / G; ++g) {
+                T xc[G];
+#pragma unroll
+                for (int j = 0; j < G; ++j) xc[j] = xn[j];
+                if (g + 1 < kSteps / G) {
+#pragma unroll
+                    for (int j = 0; j < G; ++j) xn[j] = xt[((g + 1) * G + j) * kLifChannels + tid];
+                }
+#pragma unroll
+                for (int j = 0; j < G; ++j) {
+                    const bool fired = lif_step(v, beta, th, M::in(xc[j]));
+                    spk_tile[g * G + j][tid] = spike_val<T>(fired && live);
+                }
+            }
+        } else {
+#pragma unroll 4
+            for (int tt = 0; tt < nt; ++tt) {
+                const bool fired = lif_step(v, beta, th, M::in(xt[tt * kLifChannels + tid]));
+                spk_tile[tt][tid] = spike_val<T>(fired && live);
+            }
         }
         __syncthreads();   // spike tile complete; input slot k is refilled next iteration
-        // spikes out (16-byte stores when aligned) and per-row counts from the tile
+        // spikes out (16-byte stores when aligned)
         if (vec_out) {
             for (int i = tid; i < nt * VPR; i += kLifChannels) {
                 const int tt = i / VPR, vv = i % VPR;
@@ -156,17 +195,25 @@ lif_scan_kernel(LifArgs a) {
                 if (c0 + cc < a.C) sb[(t0 + tt) * a.s_st + c0 + cc] = spk_tile[tt][cc];
             }
         }
-        // per-row spike counts; row-activity words (32 rows each) of this channel block
-        static_assert(kLifSteps <= kLifChannels && kLifSteps % 32 == 0, "one thread per tile row");
-        {
-            const int tt = tid;
-            unsigned cnt = 0;
-            if (tt < nt) {
+        // per-row spike counts from the tile; row-activity words of 32 rows
 #pragma unroll
-                for (int w = 0; w < kLifChannels / 32; ++w) cnt += __popc(row_mask[tt][w]);
+        for (int r = 0; r < kSteps / kLifChannels; ++r) {
+            const int tt = tid + r * kLifChannels;
+            int cnt = 0;
+            if (tt < nt) {
+                // each thread starts at another 16-byte column (rows are 128 or 256 B
+                // apart, so equal columns would share banks)
+                constexpr int NQ = kLifChannels * (int)sizeof(T) / 16;
+                const uint4* row = reinterpret_cast<const uint4*>(&spk_tile[tt][0]);
+#pragma unroll
+                for (int q = 0; q < NQ; ++q) {
+                    const uint4 w = row[(q + tt) & (NQ - 1)];
+                    cnt += spikes_in_word<T>(w.x) + spikes_in_word<T>(w.y) + spikes_in_word<T>(w.z) +
+                           spikes_in_word<T>(w.w);
+                }
             }
             local_count += cnt;
-            if (a.row_bits && tt < kLifSteps) {
+            if (a.row_bits) {
                 const unsigned word = __ballot_sync(0xffffffffu, cnt != 0);
                 const int64_t wi = t0 / 32 + tt / 32;
                 if (lane == 0 && wi < a.n_words) a.row_bits[((int64_t)blockIdx.x * a.B + b) * a.n_words + wi] = word;
@@ -184,13 +231,23 @@ lif_scan_kernel(LifArgs a) {
 
 }  // namespace
 
-int launch_lif_scan(int dtype, int math, const LifArgs& a, cudaStream_t stream) {
+template <int DT, int MATH>
+int launch_lif_typed(const LifArgs& a, cudaStream_t stream) {
+    using T = typename Elem<DT>::T;
+    constexpr size_t smem = LifSmem<T>::bytes;
+    auto kern = lif_scan_kernel<DT, MATH>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(NT_ERR_CUDA, "lif_scan: smem attribute: %s", cudaGetErrorString(e));
     dim3 grid((unsigned)((a.C + kLifChannels - 1) / kLifChannels), (unsigned)a.B);
-    if (dtype == NT_F32 && math == NT_F32) lif_scan_kernel<NT_F32, NT_F32><<<grid, kLifChannels, 0, stream>>>(a);
-    else if (dtype == NT_BF16 && math == NT_BF16) lif_scan_kernel<NT_BF16, NT_BF16><<<grid, kLifChannels, 0, stream>>>(a);
-    else if (dtype == NT_BF16 && math == NT_F32) lif_scan_kernel<NT_BF16, NT_F32><<<grid, kLifChannels, 0, stream>>>(a);
-    else return fail(NT_ERR_DTYPE, "lif_scan: unsupported dtype %d / math %d", dtype, math);
+    kern<<<grid, kLifChannels, smem, stream>>>(a);
     return check_launch("lif_scan_kernel");
+}
+
+int launch_lif_scan(int dtype, int math, const LifArgs& a, cudaStream_t stream) {
+    if (dtype == NT_F32 && math == NT_F32) return launch_lif_typed<NT_F32, NT_F32>(a, stream);
+    if (dtype == NT_BF16 && math == NT_BF16) return launch_lif_typed<NT_BF16, NT_BF16>(a, stream);
+    if (dtype == NT_BF16 && math == NT_F32) return launch_lif_typed<NT_BF16, NT_F32>(a, stream);
+    return fail(NT_ERR_DTYPE, "lif_scan: unsupported dtype %d / math %d", dtype, math);
 }
 
 }  // namespace nt

@@ -18,6 +18,7 @@
  *   nt_sparse_out_proj     FusedSpikeBlock._sparse_out_proj  neuratensor/core/fused.py:149-165
  *   nt_rmsnorm_in_proj     FusedSpikeBlock.norm + in_proj    neuratensor/core/fused.py:118-119
  *   nt_block_forward       FusedSpikeBlock.forward     neuratensor/core/fused.py:101-147
+ *   nt_window_attention    SlidingWindowAttention RoPE + SDPA neuratensor/core/model.py:148-178
  *   nt_lif_ssm_fused       LIF spikes driving the selective scan with given dt/B/C
  *                          (snn.py:167-182 feeding ssm.py:106-139,184-221)
  *
@@ -186,6 +187,20 @@ NT_API int nt_lif_ssm_fused(int64_t B, int64_t L, int64_t d, int64_t N,
                      const float* state_in, float* state_out,
                      void* y, void* spikes, int spike_dtype,
                      unsigned long long* spike_count, void* stream);
+
+/* Sliding-window causal attention with rotary embedding -- the middle of
+ * SlidingWindowAttention.forward (model.py:159-178: q/k/v from the qkv
+ * projection, apply_rotary on q and k (model.py:119-126), then
+ * scaled_dot_product_attention with the causal window mask j in [i-window, i]).
+ * bf16 only, head_dim 64.  qkv: [B*T, ld_qkv] rows, columns [q | k | v] of
+ * n_heads*64 each; cos_t, sin_t: [T, 64] bf16 rotary tables (the module's
+ * cached ones); out: [B*T, ld_out], head h in columns h*64 .. h*64+63 (the
+ * transpose(1,2).reshape layout o_proj takes).  Softmax scale 1/8.  RoPE
+ * rounds like the reference's bf16 ops; scores and softmax in float32, the
+ * probabilities rounded to bf16 before the product with v. */
+NT_API int nt_window_attention(int dtype, int64_t B, int64_t T, int64_t n_heads, int64_t head_dim,
+                        int64_t window, const void* qkv, int64_t ld_qkv, const void* cos_t,
+                        const void* sin_t, void* out, int64_t ld_out, void* stream);
 
 #ifdef __cplusplus
 }

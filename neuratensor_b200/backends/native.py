@@ -37,6 +37,9 @@ def _methods():
                             "forward_native": fused.FusedSpikeBlock.forward_native,
                             "_native_weights": fused.FusedSpikeBlock._native_weights,
                             "_sparse_out_proj": fused.FusedSpikeBlock._sparse_out_proj},
+        "SlidingWindowAttention": {"forward": model.SlidingWindowAttention.forward,
+                                   "forward_native": model.SlidingWindowAttention.forward_native,
+                                   "forward_torch": model.SlidingWindowAttention.forward_torch},
         "NeuraTensorModel": {"forward": model.NeuraTensorModel.forward,
                              "forward_device": model.NeuraTensorModel.forward_device,
                              "_workspace": model.NeuraTensorModel._workspace,

@@ -123,6 +123,22 @@ class SlidingWindowAttention(nn.Module):
         return self._mask
 
     def forward(self, x: Tensor) -> Tensor:
+        if x.is_cuda and x.dtype == torch.bfloat16 and self.head_dim == 64:
+            return self.forward_native(x)
+        return self.forward_torch(x)
+
+    def forward_native(self, x: Tensor) -> Tensor:
+        """RMSNorm and the projections as torch ops; RoPE, the windowed causal
+        softmax attention and the head merge in one kernel (nt_window_attention)."""
+        from .. import native
+        B, T, _ = x.shape
+        qkv = self.qkv(self.norm(x))
+        cos, sin = self.rope(qkv)                   # rows [0, T): qkv.shape[-2] == T
+        o = native.window_attention(qkv, self.n_heads, self.window, cos, sin)
+        return self.o_proj(o) + x
+
+    def forward_torch(self, x: Tensor) -> Tensor:
+        """The reference's op sequence (fp32, CPU tensors, head dims other than 64)."""
         B, T, _ = x.shape
         h = self.norm(x)
         q, k, v = self.qkv(h).view(B, T, 3, self.n_heads, self.head_dim).permute(2, 0, 3, 1, 4).unbind(0)

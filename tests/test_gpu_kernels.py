@@ -392,3 +392,42 @@ def test_block_forward_bf16_vs_oracle(nat, sparse_rows):
     np.testing.assert_allclose(N(out), ro, rtol=2e-2, atol=2e-2)
     assert agree > 0.9, agree
     assert m["spike_rate"] == pytest.approx(rm["spike_rate"], rel=2e-2)
+
+
+# --------------------------------------------------------------------------- #
+#  Sliding-window attention (model.py:148-182)                                 #
+# --------------------------------------------------------------------------- #
+
+@pytest.mark.parametrize("B,T,heads,window", [(2, 300, 2, 256), (1, 100, 3, 256), (1, 1, 2, 256),
+                                              (2, 130, 2, 32), (1, 2048, 10, 256)])
+def test_window_attention_vs_reference_ops(nat, B, T, heads, window):
+    """Native RoPE + windowed SDPA against the reference's op sequence on the same module."""
+    from neuratensor_b200.core.model import SlidingWindowAttention
+    torch.manual_seed(11)
+    att = SlidingWindowAttention(64 * heads, n_heads=heads, window=window).to(DEV).to(torch.bfloat16).eval()
+    x = torch.randn(B, T, 64 * heads, device=DEV).to(torch.bfloat16)
+    with torch.no_grad():
+        ref = att.forward_torch(x).float()
+        out = att.forward_native(x).float()
+    diff = (out - ref).abs()
+    assert diff.max().item() < 6e-2, diff.max().item()
+    assert diff.mean().item() < 4e-3, diff.mean().item()
+
+
+def test_window_attention_window_zero_is_v(nat):
+    """window 0: every query sees only its own key, so the output is v exactly."""
+    B, T, H = 2, 70, 2
+    qkv = torch.randn(B, T, 3 * 64 * H, device=DEV).to(torch.bfloat16)
+    cos = torch.randn(T, 64, device=DEV).to(torch.bfloat16)
+    sin = torch.randn(T, 64, device=DEV).to(torch.bfloat16)
+    out = nat.window_attention(qkv, H, 0, cos, sin)
+    assert torch.equal(out, qkv[:, :, 2 * 64 * H:])
+
+
+def test_window_attention_rejects_bad_args(nat):
+    qkv = torch.zeros(1, 4, 3 * 48, device=DEV, dtype=torch.bfloat16)
+    cos = torch.zeros(4, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        nat.window_attention(qkv, 1, 8, cos, cos)            # head_dim 48
+    with pytest.raises(nat.NativeError):
+        nat.window_attention(qkv.float(), 1, 8, cos, cos)    # fp32

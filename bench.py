@@ -222,6 +222,7 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     from neuratensor_b200 import InferenceEngine, NeuraTensorModel, get_preset
     from neuratensor_b200 import native
+    from neuratensor_b200.inference import ranks
     native.load()
     torch.manual_seed(SEED)
     model = NeuraTensorModel(get_preset(PRESET))
@@ -263,15 +264,8 @@ def run_ours(args):
         clocks = clk.summary()
 
         # spike metrics: NCCL gather of per-rank per-layer counts (off the timed path)
-        if world > 1:
-            allc = [torch.zeros_like(counts) for _ in range(world)]
-            dist.all_gather(allc, counts)
-            tot = torch.stack(allc).sum(0)
-            t = torch.tensor([ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        else:
-            tot = counts
+        tot = ranks.sum_counts(counts)
+        ms = ranks.max_over_ranks(ms, dev)
         di = model.config.d_model * model.config.expand
         metrics = model.metrics_from_counts(tot.tolist(), BATCH * SEQ * di * world, torch.bfloat16)
 
@@ -289,10 +283,7 @@ def run_ours(args):
             b.record(stream)
         torch.cuda.synchronize(dev)
         e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
-        if world > 1:
-            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+        e2e_ms = ranks.max_over_ranks(e2e_ms, dev)
 
         roof = None
         if rank == 0:

@@ -27,6 +27,7 @@ import json
 import os
 import statistics
 import subprocess
+import threading
 import sys
 import time
 
@@ -49,50 +50,85 @@ def _peaks():
 
 
 class Clocks:
-    """nvidia-smi sampler running while the timed region runs."""
+    """SM clock and clock-event reasons sampled every 10 ms while the timed region runs.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Read-only NVML queries (the device is matched to the CUDA device by PCI
+    address); nvidia-smi at its fastest interval when NVML is unavailable."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
     def __init__(self, device_index: int):
         self.dev = device_index
-        self.proc = None
-        self.path = os.path.join("/tmp", f"nt_clocks_{os.getpid()}.csv")
+        self.rows = []          # (sm_mhz, max_mhz, reason names)
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.dev)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        try:
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+
+    def _run_nvml(self, nv, h):
+        bits = [(name, getattr(nv, const)) for name, const in self.REASONS]
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.rows.append((float(sm), float(mx), [n for n, bit in bits if r & bit]))
+            self._stop.wait(0.01)
 
     def __enter__(self):
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            nv, h = self._nvml_handle()
+            self._thread = threading.Thread(target=self._run_nvml, args=(nv, h), daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                      "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_power_cap")
+            try:
+                self._proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={fields}",
+                                               "--format=csv,noheader,nounits", "-lms", "50"],
+                                              stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except Exception:
+                self._proc = None
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                out, _ = self._proc.communicate(timeout=5)
             except Exception:
-                self.proc.kill()
-            self.f.close()
+                self._proc.kill()
+                out = ""
+            names = [n for n, _ in self.REASONS]
+            for line in out.strip().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                try:
+                    self.rows.append((float(f[0]), float(f[1]),
+                                      [names[i] for i in range(4) if "Active" in f[2 + i] and "Not" not in f[2 + i]]))
+                except (ValueError, IndexError):
+                    pass
 
     def summary(self):
-        try:
-            rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
-        except Exception:
-            rows = []
-        if not rows:
+        if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and "Active" in r[5 + i]
-                          and "Not" not in r[5 + i]})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": sorted({n for r in self.rows for n in r[2]}), "samples": len(self.rows)}
 
 
 def cpu_baseline(budget_s: float = 20.0):
@@ -168,6 +204,14 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one ssm_scan_kernel launch of
+# this workload, from one ncu capture of `python bench.py --steps 1 --warmup 1 --no-cpu-baseline`
+# (129,039,616 read + 25,899,776 written; the o rows are partly still in L2 when the kernel ends).
+SCAN_TRAFFIC_BYTES = 154_939_392
+# the same for the standalone fused LIF -> scan op (`--workload fused-op`): 640,896,768 + 438,826,752
+FUSED_TRAFFIC_BYTES = 1_079_723_520
+
+
 def scan_roofline(model, ids, dev, peak_gbs, peak_kind, reps=20):
     """Time the selective-scan kernel on one layer of this workload with CUDA events."""
     import torch
@@ -205,8 +249,9 @@ def scan_roofline(model, ids, dev, peak_gbs, peak_kind, reps=20):
     algo = M * di * es * 4 + M * 2 * N * es + 2 * B * di * N * es   # u, dt, gate, o + B|C + state in/out
     achieved = algo / (ms * 1e-3) / 1e9
     return {"kernel": "scan_kernel (selective scan + gate, one layer)", "bound": "hbm", "achieved": achieved,
-            "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs, "traffic": None,
-            "algorithmic_bytes": algo, "ms_per_launch": ms, "peak_source": peak_kind}
+            "peak": peak_gbs, "unit": "GB/s", "frac": achieved / peak_gbs, "traffic": SCAN_TRAFFIC_BYTES,
+            "traffic_source": "ncu dram bytes of one launch", "algorithmic_bytes": algo, "ms_per_launch": ms,
+            "peak_source": peak_kind}
 
 
 def run_ours(args):
@@ -367,7 +412,7 @@ def run_standalone(args):
                       "dtype": "bf16 in / fp32 state", "data": "synthetic (seeded)",
                       "config": {"workload": "fused LIF+selective scan, B=16 L=4096 d=2304 N=64"},
                       "roofline": {"kernel": "ssm_scan_kernel (LIF fused)", "bound": "hbm", "achieved": gbs,
-                                   "peak": peak, "unit": "GB/s", "frac": gbs / peak, "traffic": None,
+                                   "peak": peak, "unit": "GB/s", "frac": gbs / peak, "traffic": FUSED_TRAFFIC_BYTES,
                                    "algorithmic_bytes": algo, "peak_source": kind},
                       "state_updates_per_s": B * L * D * N / (ms * 1e-3)})
     else:

@@ -2,10 +2,10 @@
 //
 // The recurrence is non-linear (threshold + reset), so time stays serial per
 // channel: one thread owns one (batch, channel) membrane for the whole
-// sequence.  A CTA covers kLifChannels channels of one batch row.  Input
-// tiles of kLifSteps steps x kLifChannels channels stream into a
-// kLifStages-deep shared-memory ring with cp.async, so the only latency on
-// the serial path is the membrane update itself.
+// sequence.  A CTA covers kLifChannels channels of one batch row with two
+// membrane warps and one helper warp: the helper streams input tiles into a
+// kLifStages-deep shared-memory ring with cp.async and writes the spike tiles
+// out, so the membrane warps only run the serial chain.
 //
 // Arithmetic follows the reference exactly:
 //   V = beta*V + x      -- a product then a sum, each rounded to the dtype
@@ -32,9 +32,6 @@ __device__ __forceinline__ void cp16(void* smem, const void* gmem) {
                  "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void wait_stages() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(kLifStages - 2) : "memory");
-}
 
 // Membrane update for one step.  The membrane lives in the working dtype
 // (float for fp32, bfloat16 for bf16) so the serial chain carries no
@@ -72,11 +69,12 @@ template <> __device__ __forceinline__ __nv_bfloat16 spike_val<__nv_bfloat16>(bo
 }
 
 // Shared-memory layout of one CTA: a kLifStages-deep ring of input tiles,
-// one spike tile.
+// two spike tiles, and the mbarriers that hand them between the roles.
 template <typename T> struct LifSmem {
     static constexpr int kSteps = LifSteps<T>::value;
     static constexpr size_t tile_bytes = (size_t)kSteps * kLifChannels * sizeof(T);
-    static constexpr size_t bytes = (kLifStages + 1) * tile_bytes;
+    static constexpr size_t bar_off = (kLifStages + 2) * tile_bytes;
+    static constexpr size_t bytes = bar_off + (2 * kLifStages + 4) * sizeof(uint64_t);
 };
 
 // Spikes in one 32-bit word of the spike tile: bit 7 of a bf16 1.0 (0x3F80)
@@ -85,9 +83,23 @@ template <typename T> __device__ __forceinline__ int spikes_in_word(uint32_t w);
 template <> __device__ __forceinline__ int spikes_in_word<__nv_bfloat16>(uint32_t w) { return __popc(w & 0x00800080u); }
 template <> __device__ __forceinline__ int spikes_in_word<float>(uint32_t w) { return (w >> 23) & 1u; }
 
+__device__ __forceinline__ bool lif_wait(uint64_t* bar, uint32_t parity) {
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity));
+    __syncwarp();
+    return ok;
+}
+
+// Roles: threads 0..63 (two warps) each own one channel's membrane and run
+// the serial chain; thread 64..95 (the helper warp) streams input tiles in
+// with cp.async, and writes the spike tiles out together with per-row counts
+// and row-activity words.  Input stage s and spike tile b are handed over
+// through mbarriers (in_full/in_empty, spk_full/spk_empty); every wait is
+// bounded and raises a device error flag on expiry.
+constexpr int kLifThreads = kLifChannels + 32;
+
 template <int DT, int MATH>
-__global__ void __launch_bounds__(kLifChannels)
-lif_scan_kernel(LifArgs a) {
+__global__ void __launch_bounds__(kLifThreads)
+lif_scan_kernel(LifArgs a, unsigned* err) {
     using E = Elem<DT>;
     using T = typename E::T;
     using S = typename Elem<MATH>::T;       // state / arithmetic type
@@ -97,114 +109,151 @@ lif_scan_kernel(LifArgs a) {
     constexpr int kSteps = L::kSteps;
     extern __shared__ __align__(16) unsigned char lif_smem[];
     T (*tile)[kSteps][kLifChannels] = reinterpret_cast<T (*)[kSteps][kLifChannels]>(lif_smem);
-    T (*spk_tile)[kLifChannels] = reinterpret_cast<T (*)[kLifChannels]>(lif_smem + kLifStages * L::tile_bytes);
+    T (*spk)[kSteps][kLifChannels] =
+        reinterpret_cast<T (*)[kSteps][kLifChannels]>(lif_smem + kLifStages * L::tile_bytes);
+    uint64_t* in_full = reinterpret_cast<uint64_t*>(lif_smem + L::bar_off);
+    uint64_t* in_empty = in_full + kLifStages;
+    uint64_t* spk_full = in_empty + kLifStages;
+    uint64_t* spk_empty = spk_full + 2;
 
     const int tid = threadIdx.x, lane = tid & 31;
-    const int64_t c0 = (int64_t)blockIdx.x * kLifChannels, c = c0 + tid, b = blockIdx.y;
-    const bool live = c < a.C;
-    const T* xb = static_cast<const T*>(a.x) + b * a.x_sb;
-    T* sb = static_cast<T*>(a.spikes) + b * a.s_sb;
-
-    S beta = M::from(0.f), th = M::from(0.f), v = M::from(0.f);
-    if (live) {
-        beta = M::from(E::load(static_cast<const T*>(a.beta) + c));
-        th = M::from(E::load(static_cast<const T*>(a.threshold) + c));
-        if (a.mem_in) v = M::from(E::load(static_cast<const T*>(a.mem_in) + b * a.C + c));
+    const int64_t c0 = (int64_t)blockIdx.x * kLifChannels, b = blockIdx.y;
+    const int ntiles = (int)((a.T + kSteps - 1) / kSteps);
+    if (tid == 0) {
+        for (int i = 0; i < kLifStages; ++i) {
+            mbar_init(smem_u32(&in_full[i]), 1);
+            mbar_init(smem_u32(&in_empty[i]), kLifChannels / 32);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&spk_full[i]), kLifChannels / 32);
+            mbar_init(smem_u32(&spk_empty[i]), 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // 16-byte copies when every row segment of the tile is aligned
+    __syncthreads();
+
+    if (tid < kLifChannels) {
+        // ======================= membrane warps ==============================
+        const int64_t c = c0 + tid;
+        const bool live = c < a.C;
+        S beta = M::from(0.f), th = M::from(0.f), v = M::from(0.f);
+        if (live) {
+            beta = M::from(E::load(static_cast<const T*>(a.beta) + c));
+            th = M::from(E::load(static_cast<const T*>(a.threshold) + c));
+            if (a.mem_in) v = M::from(E::load(static_cast<const T*>(a.mem_in) + b * a.C + c));
+        }
+        bool ok = true;
+        for (int k = 0; k < ntiles; ++k) {
+            const int st = k % kLifStages, sb2 = k & 1;
+            if (!lif_wait(&in_full[st], (k / kLifStages) & 1)) { ok = false; break; }
+            if (k >= 2 && !lif_wait(&spk_empty[sb2], ((k >> 1) - 1) & 1)) { ok = false; break; }
+            const T* xt = &tile[st][0][0];
+            T (*sp)[kLifChannels] = spk[sb2];
+            const int64_t t0 = (int64_t)k * kSteps;
+            const int nt = (a.T - t0 < kSteps) ? (int)(a.T - t0) : kSteps;
+            // One membrane update and one spike store per step; inputs read eight
+            // steps ahead into registers, so no shared-memory latency sits on the
+            // chain (the loads of group g+1 precede the stores of group g).
+            if (nt == kSteps) {
+                constexpr int G = 8;
+                T xn[G];
+#pragma unroll
+                for (int j = 0; j < G; ++j) xn[j] = xt[j * kLifChannels + tid];
+#pragma unroll 1
+                for (int g = 0; g < kSteps / G; ++g) {
+                    T xc[G];
+#pragma unroll
+                    for (int j = 0; j < G; ++j) xc[j] = xn[j];
+                    if (g + 1 < kSteps / G) {
+#pragma unroll
+                        for (int j = 0; j < G; ++j) xn[j] = xt[((g + 1) * G + j) * kLifChannels + tid];
+                    }
+#pragma unroll
+                    for (int j = 0; j < G; ++j) {
+                        const bool fired = lif_step(v, beta, th, M::in(xc[j]));
+                        sp[g * G + j][tid] = spike_val<T>(fired && live);
+                    }
+                }
+            } else {
+#pragma unroll 4
+                for (int tt = 0; tt < nt; ++tt) {
+                    const bool fired = lif_step(v, beta, th, M::in(xt[tt * kLifChannels + tid]));
+                    sp[tt][tid] = spike_val<T>(fired && live);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_u32(&in_empty[st]));
+                mbar_arrive(smem_u32(&spk_full[sb2]));
+            }
+        }
+        if (!ok) {
+            if (lane == 0) atomicOr(err, ERRF_TIMEOUT_EPILOGUE);
+            return;
+        }
+        if (live && a.mem_out) static_cast<T*>(a.mem_out)[b * a.C + c] = E::from_f(Elem<MATH>::to_f(v));
+        return;
+    }
+
+    // ========================= helper warp ==================================
+    const T* xb = static_cast<const T*>(a.x) + b * a.x_sb;
+    T* sbase = static_cast<T*>(a.spikes) + b * a.s_sb;
     const bool full_cols = c0 + kLifChannels <= a.C;
     const bool vec_in = full_cols && (a.x_st % EPV == 0) && (a.x_sb % EPV == 0) &&
                         ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
     const bool vec_out = full_cols && (a.s_st % EPV == 0) && (a.s_sb % EPV == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.spikes) & 15) == 0);
-    const int ntiles = (int)((a.T + kSteps - 1) / kSteps);
     constexpr int VPR = kLifChannels / EPV;      // 16-byte vectors per tile row
-
+    // input tile k into stage k % kLifStages; one commit group per tile slot
     auto issue = [&](int k) {
         if (k < ntiles) {
             T* dst = &tile[k % kLifStages][0][0];
             const int64_t t0 = (int64_t)k * kSteps;
             if (vec_in) {
-                for (int i = tid; i < kSteps * VPR; i += kLifChannels) {
+                for (int i = lane; i < kSteps * VPR; i += 32) {
                     const int tt = i / VPR, vv = i % VPR;
                     const int64_t t = t0 + tt;
                     if (t < a.T) cp16(dst + tt * kLifChannels + vv * EPV, xb + t * a.x_st + c0 + vv * EPV);
                 }
             } else {
-                for (int i = tid; i < kSteps * kLifChannels; i += kLifChannels) {
+                for (int i = lane; i < kSteps * kLifChannels; i += 32) {
                     const int tt = i / kLifChannels, cc = i % kLifChannels;
                     const int64_t t = t0 + tt;
                     dst[i] = (t < a.T && c0 + cc < a.C) ? xb[t * a.x_st + c0 + cc] : T(0.f);
                 }
             }
         }
-        commit();   // one group per tile slot (possibly empty) keeps the wait count uniform
+        commit();
     };
-
-    for (int k = 0; k < kLifStages - 1; ++k) issue(k);
     unsigned local_count = 0;
-    for (int k = 0; k < ntiles; ++k) {
-        issue(k + kLifStages - 1);
-        wait_stages();
-        __syncthreads();
-        const T* xt = &tile[k % kLifStages][0][0];
-        const int64_t t0 = (int64_t)k * kSteps;
+    // spike tile j out, its per-row counts, row-activity words; then hand it back
+    auto out = [&](int j) -> bool {
+        const int sb2 = j & 1;
+        if (!lif_wait(&spk_full[sb2], (j >> 1) & 1)) return false;
+        T (*sp)[kLifChannels] = spk[sb2];
+        const int64_t t0 = (int64_t)j * kSteps;
         const int nt = (a.T - t0 < kSteps) ? (int)(a.T - t0) : kSteps;
-        // The serial chain: one membrane update and one spike store per step.
-        // Inputs are read eight steps ahead into registers, so no shared-memory
-        // load latency sits on the chain (in program order the loads of group
-        // g+1 precede the spike stores of group g).
-        if (nt == kSteps) {
-            constexpr int G = 8;
-            T xn[G];
-#pragma unroll
-            for (int j = 0; j < G; ++j) xn[j] = xt[j * kLifChannels + tid];
-#pragma unroll 1
-            for (int g = 0; g < kSteps / G; ++g) {
-                T xc[G];
-#pragma unroll
-                for (int j = 0; j < G; ++j) xc[j] = xn[j];
-                if (g + 1 < kSteps / G) {
-#pragma unroll
-                    for (int j = 0; j < G; ++j) xn[j] = xt[((g + 1) * G + j) * kLifChannels + tid];
-                }
-#pragma unroll
-                for (int j = 0; j < G; ++j) {
-                    const bool fired = lif_step(v, beta, th, M::in(xc[j]));
-                    spk_tile[g * G + j][tid] = spike_val<T>(fired && live);
-                }
-            }
-        } else {
-#pragma unroll 4
-            for (int tt = 0; tt < nt; ++tt) {
-                const bool fired = lif_step(v, beta, th, M::in(xt[tt * kLifChannels + tid]));
-                spk_tile[tt][tid] = spike_val<T>(fired && live);
-            }
-        }
-        __syncthreads();   // spike tile complete; input slot k is refilled next iteration
-        // spikes out (16-byte stores when aligned)
         if (vec_out) {
-            for (int i = tid; i < nt * VPR; i += kLifChannels) {
+            for (int i = lane; i < nt * VPR; i += 32) {
                 const int tt = i / VPR, vv = i % VPR;
-                *reinterpret_cast<uint4*>(sb + (t0 + tt) * a.s_st + c0 + vv * EPV) =
-                    *reinterpret_cast<const uint4*>(&spk_tile[tt][vv * EPV]);
+                *reinterpret_cast<uint4*>(sbase + (t0 + tt) * a.s_st + c0 + vv * EPV) =
+                    *reinterpret_cast<const uint4*>(&sp[tt][vv * EPV]);
             }
         } else {
-            for (int i = tid; i < nt * kLifChannels; i += kLifChannels) {
+            for (int i = lane; i < nt * kLifChannels; i += 32) {
                 const int tt = i / kLifChannels, cc = i % kLifChannels;
-                if (c0 + cc < a.C) sb[(t0 + tt) * a.s_st + c0 + cc] = spk_tile[tt][cc];
+                if (c0 + cc < a.C) sbase[(t0 + tt) * a.s_st + c0 + cc] = sp[tt][cc];
             }
         }
-        // per-row spike counts from the tile; row-activity words of 32 rows
 #pragma unroll
-        for (int r = 0; r < kSteps / kLifChannels; ++r) {
-            const int tt = tid + r * kLifChannels;
+        for (int m = 0; m < kSteps / 32; ++m) {
+            const int tt = lane + 32 * m;
             int cnt = 0;
             if (tt < nt) {
-                // each thread starts at another 16-byte column (rows are 128 or 256 B
+                // each lane starts at another 16-byte column (rows are 128 or 256 B
                 // apart, so equal columns would share banks)
                 constexpr int NQ = kLifChannels * (int)sizeof(T) / 16;
-                const uint4* row = reinterpret_cast<const uint4*>(&spk_tile[tt][0]);
+                const uint4* row = reinterpret_cast<const uint4*>(&sp[tt][0]);
 #pragma unroll
                 for (int q = 0; q < NQ; ++q) {
                     const uint4 w = row[(q + tt) & (NQ - 1)];
@@ -215,14 +264,42 @@ lif_scan_kernel(LifArgs a) {
             local_count += cnt;
             if (a.row_bits) {
                 const unsigned word = __ballot_sync(0xffffffffu, cnt != 0);
-                const int64_t wi = t0 / 32 + tt / 32;
+                const int64_t wi = t0 / 32 + m;
                 if (lane == 0 && wi < a.n_words) a.row_bits[((int64_t)blockIdx.x * a.B + b) * a.n_words + wi] = word;
             }
         }
-        __syncthreads();   // spike tile is rewritten by the next tile
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&spk_empty[sb2]));
+        return true;
+    };
+
+    // Tile j is announced (in_full) as soon as it has landed, one tile ahead of
+    // the membrane warps; commit groups: one per tile slot, tiles in order.
+    static_assert(kLifStages == 3, "wait_group counts below assume three stages");
+    for (int k = 0; k < kLifStages; ++k) issue(k);
+    asm volatile("cp.async.wait_group 2;" ::: "memory");                  // tile 0 has landed
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&in_full[0]));
+    bool ok = true;
+    for (int k = 0; k < ntiles && ok; ++k) {
+        if (k + 1 < ntiles) {
+            asm volatile("cp.async.wait_group 1;" ::: "memory");          // tiles up to k+1 have landed
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&in_full[(k + 1) % kLifStages]));
+        }
+        if (k >= 1 && !out(k - 1)) { ok = false; break; }
+        // stage k % kLifStages takes tile k + kLifStages once the membrane warps are done with tile k
+        if (k + kLifStages < ntiles) {
+            if (!lif_wait(&in_empty[k % kLifStages], (k / kLifStages) & 1)) { ok = false; break; }
+        }
+        issue(k + kLifStages);
     }
+    if (ok && ntiles > 0 && !out(ntiles - 1)) ok = false;
     asm volatile("cp.async.wait_all;" ::: "memory");
-    if (live && a.mem_out) static_cast<T*>(a.mem_out)[b * a.C + c] = E::from_f(Elem<MATH>::to_f(v));
+    if (!ok) {
+        if (lane == 0) atomicOr(err, ERRF_TIMEOUT_PRODUCER);
+        return;
+    }
     if (a.spike_count) {
         const unsigned wsum = __reduce_add_sync(0xffffffffu, local_count);
         if (lane == 0 && wsum) atomicAdd(a.spike_count, (unsigned long long)wsum);
@@ -238,8 +315,10 @@ int launch_lif_typed(const LifArgs& a, cudaStream_t stream) {
     auto kern = lif_scan_kernel<DT, MATH>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "lif_scan: smem attribute: %s", cudaGetErrorString(e));
+    int dev = 0;
+    cudaGetDevice(&dev);
     dim3 grid((unsigned)((a.C + kLifChannels - 1) / kLifChannels), (unsigned)a.B);
-    kern<<<grid, kLifChannels, smem, stream>>>(a);
+    kern<<<grid, kLifThreads, smem, stream>>>(a, device_error_word(dev));
     return check_launch("lif_scan_kernel");
 }
 

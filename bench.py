@@ -1,13 +1,13 @@
-"""Benchmark: small-preset bf16 prefill (B=8 per GPU, L=2048) through the B200 kernels.
+"""Benchmark: small-preset bf16 prefill (batch 8 x L=2048) through the B200 kernels.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One step = one ``NeuraTensorModel`` forward (12 FusedSpikeBlocks, 2 sliding-
 window attention layers, tied lm_head) over a [8, 2048] batch of uniform
 random token ids, with the per-layer spike metrics read back.  Weights are
-random-init from a seed.  With N GPUs (torchrun) every rank runs its own
-batch of 8 sequences (sequences are independent: weak scaling, no collective
-on the data path); NCCL only gathers the per-rank spike counts.
+random-init from a seed.  With N GPUs (torchrun) the same 8 sequences are
+split across the ranks (sequences are independent: strong scaling, no
+collective on the data path); NCCL only gathers the per-rank spike counts.
 
 Printed JSON (rank 0): ``value`` = tokens/s over all ranks with inputs
 already in HBM, timed with CUDA events per step (max over ranks), L2 flushed
@@ -35,7 +35,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 PRESET = "small"
-BATCH = 8
+GLOBAL_BATCH = 8          # sequences in the whole job, split across the ranks
 SEQ = 2048
 SEED = 1234
 
@@ -273,9 +273,13 @@ def run_ours(args):
     model = NeuraTensorModel(get_preset(PRESET))
     eng = InferenceEngine(model, device=f"cuda:{local}", dtype=torch.bfloat16)
     model = eng.model
-    g = torch.Generator().manual_seed(SEED + rank)
-    host_ids = [torch.randint(0, model.config.vocab_size, (BATCH, SEQ), generator=g).pin_memory()
-                for _ in range(2)]
+    # the same global batch at every world size; this rank runs rows [start, stop)
+    start, stop = ranks.batch_shard(GLOBAL_BATCH, world, rank)
+    if stop <= start:
+        raise SystemExit(f"{world} ranks for {GLOBAL_BATCH} sequences: rank {rank} would get none")
+    g = torch.Generator().manual_seed(SEED)
+    host_ids = [torch.randint(0, model.config.vocab_size, (GLOBAL_BATCH, SEQ), generator=g)[start:stop]
+                .contiguous().pin_memory() for _ in range(2)]
     dev_ids = [h.to(dev) for h in host_ids]
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -312,7 +316,7 @@ def run_ours(args):
         tot = ranks.sum_counts(counts)
         ms = ranks.max_over_ranks(ms, dev)
         di = model.config.d_model * model.config.expand
-        metrics = model.metrics_from_counts(tot.tolist(), BATCH * SEQ * di * world, torch.bfloat16)
+        metrics = model.metrics_from_counts(tot.tolist(), GLOBAL_BATCH * SEQ * di, torch.bfloat16)
 
         # end to end through the public API: pinned host ids -> run() -> metrics on the host
         e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -340,19 +344,20 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    tokens = BATCH * SEQ * world * args.steps
+    tokens = GLOBAL_BATCH * SEQ * args.steps
     value = tokens / (ms / 1000.0)
     e2e_value = tokens / (e2e_ms / 1000.0)
     cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
     line = {
         "metric": "tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random ids, random-init weights, seeded)",
-        "config": {"workload": f"small preset bf16 prefill, B={BATCH} per GPU x L={SEQ}", "preset": PRESET,
-                   "global_batch": BATCH * world, "seq_len": SEQ, "parallelism": f"dp{world} (batch shards)",
+        "config": {"workload": f"small preset bf16 prefill, batch {GLOBAL_BATCH} x L={SEQ} split across the GPUs",
+                   "preset": PRESET, "global_batch": GLOBAL_BATCH, "per_gpu_batch": stop - start, "seq_len": SEQ,
+                   "parallelism": f"dp{world} (batch shards)",
                    "l2": "flushed (256 MiB write) before every timed step"},
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * SEQ * 8,
-                "d2h_bytes_per_step": 8 * model.config.n_layers},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": GLOBAL_BATCH * SEQ * 8,
+                "d2h_bytes_per_step": 8 * model.config.n_layers * world},
         "gpu_launches": launches,
         "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
         "spike_rate": metrics["spike_rate"],

@@ -118,6 +118,8 @@ struct BlockWs {
     void *xn, *h, *gate, *spikes, *dt, *bc, *o;
     unsigned* row_bits;
     int *pos, *idx, *counters;
+    void* scanseg;              // float32 end states / decays / carry-ins of the segmented scan
+    size_t scanseg_bytes;
     int64_t bytes;
 };
 BlockWs block_ws(void* ws, int dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N) {
@@ -136,6 +138,8 @@ BlockWs block_ws(void* ws, int dtype, int64_t B, int64_t T, int64_t dm, int64_t 
     w.pos = c.take<int>(M * 4);
     w.idx = c.take<int>(M * 4);
     w.counters = c.take<int>(64);
+    w.scanseg_bytes = selective_scan_segmented_workspace(B, T, di, N);
+    w.scanseg = w.scanseg_bytes ? c.take<char>((int64_t)w.scanseg_bytes) : nullptr;
     w.bytes = c.off;
     return w;
 }
@@ -370,7 +374,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         const char* bc = static_cast<const char*>(w.bc);
         ScanArgs a{B, T, di, N, w.spikes, w.dt, bc, bc + N * es, 2 * N, log_A, D, w.gate, state_in, state_out, w.o,
                    w.pos, w.counters + 1, /*gate_is_silu=*/1};
-        NT_TRY(launch_selective_scan(dtype, state_dtype, a, st));
+        NT_TRY(launch_selective_scan_segmented(dtype, state_dtype, a, w.scanseg, w.scanseg_bytes, st));
     }
     // (c) out_proj on the processed rows, * out_scale + residual, scattered back
     {

@@ -35,8 +35,15 @@ struct ScanArgs {
     // (inactive rows are skipped).
     const int* row_pos; const int* sparse_flag;
     int gate_is_silu;                       // gate already holds rnd(silu(gate))
+    float* seg_decay;                       // state-only segment pass: exp(A*sum(dt)) per state
 };
 int launch_selective_scan(int dtype, int state_dtype, const ScanArgs& a, cudaStream_t stream);
+// Time-segmented variant for small batches (needs the float32 workspace below;
+// falls back to launch_selective_scan when one segment suffices).
+int scan_segments(int64_t B, int64_t T);
+size_t selective_scan_segmented_workspace(int64_t B, int64_t T, int64_t d, int64_t N);
+int launch_selective_scan_segmented(int dtype, int state_dtype, const ScanArgs& a, void* ws, size_t ws_bytes,
+                                    cudaStream_t stream);
 
 struct FusedArgs {
     int64_t B, L, d, N;

@@ -33,6 +33,7 @@
 // On the fast path A is exactly (n+1)*A[c,0].
 #include "nt_kernels.cuh"
 
+#include <algorithm>
 #include <type_traits>
 
 namespace nt {
@@ -167,9 +168,14 @@ __device__ __forceinline__ void widen16(const __nv_bfloat16* src, float* v) {
 // latency-bound, so warps per SM matter more than hoisting further ahead).
 template <int NPT> struct ScanMinBlocks { static constexpr int value = NPT == 8 ? NT_SCAN_MINB8 : NT_SCAN_MINB4; };
 
-template <int DT, int SDT, int TPC, int NPT, int MODE>
+// OUT = 0 (MODE 0 only): the state-only pass of the time-segmented scan --
+// no C, no outputs; writes the segment's end state (float32, from a zero
+// start) to state_out and its total decay exp(A*sum(dt)) per state to
+// a.seg_decay, with the same A the recurrence used.
+template <int DT, int SDT, int TPC, int NPT, int MODE, int OUT = 1>
 __global__ void __launch_bounds__(128, ScanMinBlocks<NPT>::value)
 ssm_scan_kernel(ScanArgs a, FusedArgs f) {
+    static_assert(OUT == 1 || MODE == 0, "state-only pass is a MODE 0 variant");
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
     using L = ScanSmem<TPC, NPT, T, MODE>;
     constexpr int CPB = L::CPB, NP = L::NP, kTch = L::TCH, NPR = NPT / 2;
@@ -255,6 +261,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         lim2[j] = make_float2((lim_mask >> (2 * j)) & 1u ? 1.f : 0.f, (lim_mask >> (2 * j + 1)) & 1u ? 1.f : 0.f);
     }
     float beta = 0.f, th = 0.f, mem = 0.f;
+    float dt_sum = 0.f;                          // state-only pass: sum of dt over the segment
     if (MODE == 1 && live) {
         beta = f.beta[c];
         th = f.threshold[c];
@@ -289,7 +296,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         stage_tile<T, CPB, kTch>(r_dt, p_dt + row0 * d, d, t0, T_len, c0, d, act_vec, tid);
         if (has_gate) stage_tile<T, CPB, kTch>(r_g, p_g + row0 * d, d, t0, T_len, c0, d, act_vec, tid);
         stage_tile<T, NP, kTch>(r_B, p_B + row0 * ld_bc, ld_bc, t0, T_len, 0, N, bc_vec, tid);
-        stage_tile<T, NP, kTch>(r_C, p_C + row0 * ld_bc, ld_bc, t0, T_len, 0, N, bc_vec, tid);
+        if (OUT) stage_tile<T, NP, kTch>(r_C, p_C + row0 * ld_bc, ld_bc, t0, T_len, 0, N, bc_vec, tid);
         cp_async_commit();
     };
 
@@ -306,9 +313,11 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         for (int q = 0; q < NPT / 4; ++q) {
             const int n4 = bc_swz<NP>(sub * NPT + 4 * q);
             const float4 bq = *reinterpret_cast<const float4*>(w_B + tt * NP + n4);
-            const float4 cq = *reinterpret_cast<const float4*>(w_C + tt * NP + n4);
             Bf[4 * q] = bq.x; Bf[4 * q + 1] = bq.y; Bf[4 * q + 2] = bq.z; Bf[4 * q + 3] = bq.w;
-            Cf[4 * q] = cq.x; Cf[4 * q + 1] = cq.y; Cf[4 * q + 2] = cq.z; Cf[4 * q + 3] = cq.w;
+            if (OUT) {
+                const float4 cq = *reinterpret_cast<const float4*>(w_C + tt * NP + n4);
+                Cf[4 * q] = cq.x; Cf[4 * q + 1] = cq.y; Cf[4 * q + 2] = cq.z; Cf[4 * q + 3] = cq.w;
+            }
         }
         const float2 ud = w_ud[tt * CPB + cl];
         float u;
@@ -361,11 +370,16 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         }
 #pragma unroll
         for (int j = 0; j < NPR; ++j) { h[2 * j] = hv[j].x; h[2 * j + 1] = hv[j].y; }
-        // C.h as one packed fma chain, then one add of the two lanes
-        float2 y2 = __fmul2_rn(make_float2(Cf[0], Cf[1]), hv[0]);
+        if constexpr (OUT) {
+            // C.h as one packed fma chain, then one add of the two lanes
+            float2 y2 = __fmul2_rn(make_float2(Cf[0], Cf[1]), hv[0]);
 #pragma unroll
-        for (int j = 1; j < NPR; ++j) y2 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y2);
-        yp_out = y2.x + y2.y;
+            for (int j = 1; j < NPR; ++j) y2 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y2);
+            yp_out = y2.x + y2.y;
+        } else {
+            yp_out = 0.f;
+            dt_sum += dtv;                         // the segment's total decay exponent
+        }
         u_out = u;
     };
 
@@ -393,7 +407,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         for (int i = tid * EPV; i < kTch * NP; i += 128 * EPV) {
             float bv[EPV], cv[EPV];
             widen16(rb + 3 * kTch * CPB + i, bv);
-            widen16(rb + 3 * kTch * CPB + kTch * NP + i, cv);
+            if (OUT) widen16(rb + 3 * kTch * CPB + kTch * NP + i, cv);
 #pragma unroll
             for (int k = 0; k < EPV; k += 4) {
                 const int tt = (i + k) / NP, n = (i + k) % NP;     // four states of one row
@@ -404,7 +418,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                     b4.x *= r4.x; b4.y *= r4.y; b4.z *= r4.z; b4.w *= r4.w;
                 }
                 *reinterpret_cast<float4*>(w_B + o) = b4;
-                *reinterpret_cast<float4*>(w_C + o) = make_float4(cv[k], cv[k + 1], cv[k + 2], cv[k + 3]);
+                if (OUT) *reinterpret_cast<float4*>(w_C + o) = make_float4(cv[k], cv[k + 1], cv[k + 2], cv[k + 3]);
             }
         }
         if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
@@ -418,13 +432,16 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             float ypr[kRun], upr[kRun];
             if (hippo) static_for<0, kRun>([&](auto j) { constexpr int q = decltype(j)::value; step(r0 + q, nt, std::true_type{}, ypr[q], upr[q]); });
             else static_for<0, kRun>([&](auto j) { constexpr int q = decltype(j)::value; step(r0 + q, nt, std::false_type{}, ypr[q], upr[q]); });
+            if constexpr (OUT) {
 #pragma unroll
-            for (int q = 0; q < kRun; ++q) {
-                w_yp[(r0 + q) * 128 + yp_slot<TPC>(r0 + q, cl, sub)] = ypr[q];
-                if (MODE == 1) w_s[(r0 + q) * CPB + cl] = upr[q];   // every thread of the channel stores the same value
+                for (int q = 0; q < kRun; ++q) {
+                    w_yp[(r0 + q) * 128 + yp_slot<TPC>(r0 + q, cl, sub)] = ypr[q];
+                    if (MODE == 1) w_s[(r0 + q) * CPB + cl] = upr[q];   // every thread of the channel stores the same value
+                }
             }
         });
         __syncthreads();
+        if constexpr (OUT) {
         // ---- reduce partial sums, D*u, gate; coalesced stores -----------------
         // thread tid covers channel tid % CPB of steps tid / CPB + k*TPC
 #pragma unroll 1
@@ -480,9 +497,25 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                 spike_local += (uu != 0.f);
             }
         }
+        }   // OUT
         __syncthreads();   // raw_buf(kc) is refilled by the next iteration's issue
     }
     // ---- carry-out -----------------------------------------------------------
+    if constexpr (!OUT) {
+        // end state of the segment (float32) and its decay exp(A*sum(dt)) per state
+        if (live) {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int64_t n = (int64_t)sub * NPT + j;
+                if (n >= N) continue;
+                const int64_t si = (b * d + c) * N + n;
+                const float a2 = hippo ? (float)(n + 1) * Abase * kLog2e : A2[j];
+                static_cast<float*>(a.state_out)[si] = h[j];
+                a.seg_decay[si] = ex2(a2 * dt_sum);
+            }
+        }
+        return;
+    }
     void* sout = MODE ? (void*)f.state_out : a.state_out;
     if (live && sout) {
 #pragma unroll
@@ -509,11 +542,11 @@ int pow2_at_least(int64_t x) {
     return p;
 }
 
-template <int DT, int SDT, int MODE, int TPC, int NPT>
+template <int DT, int SDT, int MODE, int TPC, int NPT, int OUT>
 int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
     using L = ScanSmem<TPC, NPT, T, MODE>;
-    auto kern = ssm_scan_kernel<DT, SDT, TPC, NPT, MODE>;
+    auto kern = ssm_scan_kernel<DT, SDT, TPC, NPT, MODE, OUT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
     const int64_t d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
@@ -528,7 +561,7 @@ int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
 // States per thread: 8, or 4 when 8 would leave the GPU with fewer than four
 // 128-thread CTAs per SM (the recurrence is latency-bound, so warps matter
 // more than the extra per-thread work of a narrower state slice).
-template <int DT, int SDT, int MODE>
+template <int DT, int SDT, int MODE, int OUT = 1>
 int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     const int64_t N = MODE ? f.N : a.N, d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
     if (N > 256) return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)N);
@@ -539,26 +572,56 @@ int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     const bool narrow = N >= 8 && tpc8 <= 16 && ctas8 < (int64_t)NT_SCAN_NARROW_CTAS * sms;
     if (narrow) {
         switch (pow2_at_least((N + 3) / 4)) {
-            case 2: return launch_tpc<DT, SDT, MODE, 2, 4>(a, f, stream);
-            case 4: return launch_tpc<DT, SDT, MODE, 4, 4>(a, f, stream);
-            case 8: return launch_tpc<DT, SDT, MODE, 8, 4>(a, f, stream);
-            case 16: return launch_tpc<DT, SDT, MODE, 16, 4>(a, f, stream);
-            case 32: return launch_tpc<DT, SDT, MODE, 32, 4>(a, f, stream);
+            case 2: return launch_tpc<DT, SDT, MODE, 2, 4, OUT>(a, f, stream);
+            case 4: return launch_tpc<DT, SDT, MODE, 4, 4, OUT>(a, f, stream);
+            case 8: return launch_tpc<DT, SDT, MODE, 8, 4, OUT>(a, f, stream);
+            case 16: return launch_tpc<DT, SDT, MODE, 16, 4, OUT>(a, f, stream);
+            case 32: return launch_tpc<DT, SDT, MODE, 32, 4, OUT>(a, f, stream);
             default: break;
         }
     }
     switch (tpc8) {
-        case 1: return launch_tpc<DT, SDT, MODE, 1, 8>(a, f, stream);
-        case 2: return launch_tpc<DT, SDT, MODE, 2, 8>(a, f, stream);
-        case 4: return launch_tpc<DT, SDT, MODE, 4, 8>(a, f, stream);
-        case 8: return launch_tpc<DT, SDT, MODE, 8, 8>(a, f, stream);
-        case 16: return launch_tpc<DT, SDT, MODE, 16, 8>(a, f, stream);
-        case 32: return launch_tpc<DT, SDT, MODE, 32, 8>(a, f, stream);
+        case 1: return launch_tpc<DT, SDT, MODE, 1, 8, OUT>(a, f, stream);
+        case 2: return launch_tpc<DT, SDT, MODE, 2, 8, OUT>(a, f, stream);
+        case 4: return launch_tpc<DT, SDT, MODE, 4, 8, OUT>(a, f, stream);
+        case 8: return launch_tpc<DT, SDT, MODE, 8, 8, OUT>(a, f, stream);
+        case 16: return launch_tpc<DT, SDT, MODE, 16, 8, OUT>(a, f, stream);
+        case 32: return launch_tpc<DT, SDT, MODE, 32, 8, OUT>(a, f, stream);
         default: return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)N);
     }
 }
 
 }  // namespace
+
+template <int DT>
+int launch_segmented(int state_dtype, const ScanArgs& a, int S, float* ws, cudaStream_t stream);
+
+// Segments: for one or two rows, the largest power of two S with B*S <= 8, T
+// divisible by S and at least 128 steps per segment (1: no segmentation).
+// Measured on the small preset (T = 2048): B=1 2.79 ms per forward with 8
+// segments (3.79 without), B=2 3.91 ms with 4 (4.56), B=4 slower with 2.
+int scan_segments(int64_t B, int64_t T) {
+    if (B > 2) return 1;
+    int S = 1;
+    while (B * S * 2 <= 8 && T % (S * 2) == 0 && T / (S * 2) >= 128) S *= 2;
+    return S;
+}
+
+size_t selective_scan_segmented_workspace(int64_t B, int64_t T, int64_t d, int64_t N) {
+    const int S = scan_segments(B, T);
+    return S > 1 ? 3 * (size_t)(B * S) * (size_t)d * (size_t)N * sizeof(float) : 0;
+}
+
+int launch_selective_scan_segmented(int dtype, int state_dtype, const ScanArgs& a, void* ws, size_t ws_bytes,
+                                    cudaStream_t stream) {
+    const int S = scan_segments(a.B, a.T);
+    if (S == 1 || !ws || ws_bytes < selective_scan_segmented_workspace(a.B, a.T, a.d, a.N))
+        return launch_selective_scan(dtype, state_dtype, a, stream);
+    if (dtype == NT_F32 && state_dtype == NT_F32) return launch_segmented<NT_F32>(state_dtype, a, S, static_cast<float*>(ws), stream);
+    if (dtype == NT_BF16 && (state_dtype == NT_F32 || state_dtype == NT_BF16))
+        return launch_segmented<NT_BF16>(state_dtype, a, S, static_cast<float*>(ws), stream);
+    return fail(NT_ERR_DTYPE, "selective_scan: unsupported dtype %d / state dtype %d", dtype, state_dtype);
+}
 
 int launch_selective_scan(int dtype, int state_dtype, const ScanArgs& a, cudaStream_t stream) {
     FusedArgs f{};
@@ -566,6 +629,63 @@ int launch_selective_scan(int dtype, int state_dtype, const ScanArgs& a, cudaStr
     if (dtype == NT_BF16 && state_dtype == NT_F32) return launch_mode<NT_BF16, NT_F32, 0>(a, f, stream);
     if (dtype == NT_BF16 && state_dtype == NT_BF16) return launch_mode<NT_BF16, NT_BF16, 0>(a, f, stream);
     return fail(NT_ERR_DTYPE, "selective_scan: unsupported dtype %d / state dtype %d", dtype, state_dtype);
+}
+
+// ---------------------------------------------------------------------------
+// Time-segmented scan for small batches.  With B rows the plain scan has
+// B*d/CPB CTAs, each walking all T steps; splitting T into S segments gives
+// S times the CTAs and S times shorter serial chains:
+//   A. state-only pass over every segment from a zero state: its end state
+//      and its decay exp(A*sum(dt)) per state;
+//   B. carry-in of segment s: h_in[0] = state_in,
+//      h_in[s+1] = end[s] + decay[s] * h_in[s]  (the recurrence is linear in h);
+//      h_in after the last segment is the returned state;
+//   C. the ordinary scan of every segment from its h_in, writing the outputs.
+// Segments are consecutive row ranges of one sequence, so a (row, segment)
+// pair is handled as a "batch row" of length T/S at rows (b*S + s)*T/S.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) scan_seg_combine_kernel(int64_t B, int S, int64_t dN, const float* h_end,
+                                                              const float* decay, const void* state_in, int sin_bf16,
+                                                              float* h_in, void* state_out, int sout_bf16) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < B * dN; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / dN, j = i % dN;
+        float h = 0.f;
+        if (state_in) h = sin_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(state_in)[i])
+                                   : static_cast<const float*>(state_in)[i];
+        for (int s = 0; s < S; ++s) {
+            const int64_t v = (b * S + s) * dN + j;
+            h_in[v] = h;
+            h = fmaf(decay[v], h, h_end[v]);
+        }
+        if (state_out) {
+            if (sout_bf16) static_cast<__nv_bfloat16*>(state_out)[i] = __float2bfloat16_rn(h);
+            else static_cast<float*>(state_out)[i] = h;
+        }
+    }
+}
+
+template <int DT>
+int launch_segmented(int state_dtype, const ScanArgs& a, int S, float* ws, cudaStream_t stream) {
+    FusedArgs f{};
+    const int64_t Ts = a.T / S, Bs = a.B * S, n_st = Bs * a.d * a.N;
+    float* h_end = ws;
+    float* decay = h_end + n_st;
+    float* h_in = decay + n_st;
+    ScanArgs pa = a;                               // A: state-only, zero start
+    pa.B = Bs; pa.T = Ts; pa.state_in = nullptr; pa.state_out = h_end; pa.seg_decay = decay;
+    pa.gate = nullptr; pa.y = nullptr; pa.row_pos = nullptr; pa.sparse_flag = nullptr;
+    int rc = launch_mode<DT, NT_F32, 0, 0>(pa, f, stream);
+    if (rc != NT_OK) return rc;
+    const int64_t dN = a.d * a.N;                  // B: carry-in per segment, returned state
+    const int64_t blocks = std::min<int64_t>((a.B * dN + 255) / 256, 148 * 8);
+    scan_seg_combine_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a.B, S, dN, h_end, decay, a.state_in,
+                                                                  state_dtype == NT_BF16, h_in, a.state_out,
+                                                                  state_dtype == NT_BF16);
+    rc = check_launch("scan_seg_combine_kernel");
+    if (rc != NT_OK) return rc;
+    ScanArgs pc = a;                               // C: outputs from the carry-in
+    pc.B = Bs; pc.T = Ts; pc.state_in = h_in; pc.state_out = nullptr;
+    return launch_mode<DT, NT_F32, 0, 1>(pc, f, stream);
 }
 
 int launch_lif_ssm_fused(const FusedArgs& f, cudaStream_t stream) {

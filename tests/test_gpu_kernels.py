@@ -431,3 +431,31 @@ def test_window_attention_rejects_bad_args(nat):
         nat.window_attention(qkv, 1, 8, cos, cos)            # head_dim 48
     with pytest.raises(nat.NativeError):
         nat.window_attention(qkv.float(), 1, 8, cos, cos)    # fp32
+
+
+def test_block_forward_fp32_time_segmented_scan(nat):
+    """B=1 with T=512 takes the time-segmented scan (4 segments of 128 steps):
+    outputs and carried state against the oracle, from a zero and from a
+    non-zero carry-in."""
+    from neuratensor_b200 import FusedSpikeBlock
+    from neuratensor_b200.core.fused import BlockState
+    torch.manual_seed(21)
+    blk = FusedSpikeBlock(d_model=32, d_state=16, expand=2)
+    with torch.no_grad():
+        blk.ssm.dt_proj.bias.normal_(-1.5, 0.5)          # dt ~ 0.2: the scan matters
+    blk = blk.to(DEV).eval()
+    p = O.params_from_state_dict(blk.state_dict())
+    rng = np.random.default_rng(22)
+    x = rng.normal(0, 1.0, (1, 512, 32)).astype(np.float32)
+    di, N_ = 64, 16
+    mem0 = rng.normal(0, 0.3, (1, di)).astype(np.float32)
+    st0 = rng.normal(0, 0.3, (1, di, N_)).astype(np.float32)
+    for with_state in (False, True):
+        ost = O.OracleState(membrane=mem0, ssm_state=st0) if with_state else None
+        ro, rst, _ = O.block_forward(x, p, ost, "fp32")
+        state = BlockState(membrane=T(mem0), ssm_state=T(st0)) if with_state else None
+        with torch.no_grad():
+            out, st, _ = blk(T(x), state)
+        np.testing.assert_allclose(N(out), ro, rtol=1e-4, atol=2e-5)
+        np.testing.assert_allclose(N(st.ssm_state), rst.ssm_state, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(N(st.membrane), rst.membrane, rtol=1e-5, atol=1e-6)

@@ -201,7 +201,8 @@ class NeuraTensorModel(nn.Module):
             self._ws = torch.empty(n, dtype=torch.uint8, device=x.device)
         return self._ws
 
-    def forward_device(self, input_ids: Tensor, states: Optional[List[Optional[BlockState]]] = None):
+    def forward_device(self, input_ids: Tensor, states: Optional[List[Optional[BlockState]]] = None,
+                       workspace: Optional[Tensor] = None):
         """Forward without any host sync: returns (logits, states, per-layer spike counts on device)."""
         if states is None:
             states = [None] * len(self.blocks)
@@ -212,7 +213,7 @@ class NeuraTensorModel(nn.Module):
             input_ids = input_ids[:, : self.config.max_seq_len]
         x = self.embedding(input_ids)
         counts = torch.zeros(len(self.blocks), dtype=torch.int64, device=x.device)
-        ws = self._workspace(x)
+        ws = workspace if workspace is not None else self._workspace(x)
         new_states: List[BlockState] = []
         with torch.no_grad():
             for i, (blk, st) in enumerate(zip(self.blocks, states)):
@@ -245,15 +246,38 @@ class NeuraTensorModel(nn.Module):
         return sum(p.numel() for p in self.parameters() if p.requires_grad)
 
     @torch.no_grad()
+    def decode_graph(self, batch: int, device, dtype):
+        """The captured single-token step for this batch size.  A graph holds raw
+        addresses, so it is rebuilt when a parameter changes (version or storage)
+        or an attention layer's RoPE tables were rebuilt."""
+        from ..inference.decode import DecodeGraph
+        sig = (tuple((p.data_ptr(), p._version) for p in self.parameters()),
+               tuple((a.rope.cos_cached.data_ptr(), a.rope.sin_cached.data_ptr()) for a in self.attn_layers.values()))
+        key = (batch, str(device), dtype)
+        cache = self.__dict__.setdefault("_decode_graphs", {})
+        if key not in cache or cache[key][0] != sig:
+            cache.pop(key, None)
+            cache[key] = (sig, DecodeGraph(self, batch, torch.device(device), dtype))
+        return cache[key][1]
+
     def generate(self, input_ids: Tensor, max_new_tokens: int = 50, temperature: float = 1.0, top_k: int = 50,
                  top_p: float = 1.0, repetition_penalty: float = 1.0, stop_tokens: Optional[List[int]] = None,
-                 states: Optional[List[Optional[BlockState]]] = None) -> Tuple[Tensor, List[BlockState]]:
-        """Autoregressive sampling with carried block state (model.py:301-370)."""
+                 states: Optional[List[Optional[BlockState]]] = None,
+                 use_graph: bool = True) -> Tuple[Tensor, List[BlockState]]:
+        """Autoregressive sampling with carried block state (model.py:301-370).
+
+        On CUDA the per-token steps replay one captured graph of the whole model
+        (``inference/decode.py``); ``use_graph=False`` runs them one launch at a
+        time.  Both run the same kernels on the same inputs."""
         self.eval()
         out = input_ids
         stop = set(stop_tokens or [])
         logits, states, _ = self.forward_device(out, states)
         nxt_logits = logits[:, -1, :]
+        graph = None
+        if use_graph and out.is_cuda and max_new_tokens > 1:
+            graph = self.decode_graph(out.shape[0], out.device, logits.dtype)
+            graph.load_states(states)
         for _ in range(max_new_tokens):
             if repetition_penalty != 1.0:
                 for b in range(out.shape[0]):
@@ -275,8 +299,13 @@ class NeuraTensorModel(nn.Module):
             out = torch.cat([out, tok], dim=1)
             if stop and tok.item() in stop:
                 break
-            logits, states, _ = self.forward_device(tok, states)
-            nxt_logits = logits[:, -1, :]
+            if graph is not None:
+                nxt_logits = graph.step(tok).clone()
+            else:
+                logits, states, _ = self.forward_device(tok, states)
+                nxt_logits = logits[:, -1, :]
+        if graph is not None:
+            states = graph.states()
         return out, states
 
     def info(self) -> str:

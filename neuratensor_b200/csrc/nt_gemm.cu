@@ -515,15 +515,32 @@ static int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     return check_launch("gemm_tc_kernel");
 }
 
-// Tile width: the candidate that wastes the fewest columns of N (ties go to
-// the wider tile, which re-reads A fewer times).
-static int pick_bn(int64_t N) {
-    static const int cand[] = {256, 224, 192, 160, 128};
-    int best = 128;
+#ifndef NT_GEMM_TILE_OVERHEAD
+#define NT_GEMM_TILE_OVERHEAD 64
+#endif
+// Tile width for an M x N output on `sms` persistent CTAs.  First choice:
+// the candidate that wastes the fewest columns of N (ties go to the wider
+// tile, which re-reads A fewer times).  When that leaves fewer than two tiles
+// per CTA (small M), the candidate with the smallest modelled time instead:
+// waves * (BN + overhead), a wave being one tile per CTA and the overhead (in
+// columns) a tile's fixed cost (pipeline fill, epilogue tail).
+static int pick_bn(int64_t M, int64_t N, int sms) {
+    static const int cand[] = {256, 224, 192, 160, 128, 96, 64};
+    const int64_t m_tiles = (M + kBM - 1) / kBM;
+    int pad_best = 128;
     int64_t best_pad = -1;
     for (int bn : cand) {
+        if (bn < 128) continue;
         const int64_t pad = ((N + bn - 1) / bn) * bn - N;
-        if (best_pad < 0 || pad < best_pad) { best = bn; best_pad = pad; }
+        if (best_pad < 0 || pad < best_pad) { pad_best = bn; best_pad = pad; }
+    }
+    if (m_tiles * ((N + pad_best - 1) / pad_best) >= 2LL * sms) return pad_best;
+    int best = pad_best;
+    int64_t best_cost = -1;
+    for (int bn : cand) {
+        const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
+        const int64_t cost = ((tiles + sms - 1) / sms) * (bn + NT_GEMM_TILE_OVERHEAD);
+        if (best_cost < 0 || cost < best_cost) { best = bn; best_cost = cost; }
     }
     return best;
 }
@@ -531,12 +548,16 @@ static int pick_bn(int64_t N) {
 template <int KIND>
 static int launch_kind(int dtype, const GemmArgs& g, cudaStream_t stream) {
     if (dtype == NT_BF16) {
-        switch (pick_bn(g.N)) {
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        switch (pick_bn(g.M, g.N, sms)) {
             case 256: return launch_tc<KIND, 256>(g, stream);
             case 224: return launch_tc<KIND, 224>(g, stream);
             case 192: return launch_tc<KIND, 192>(g, stream);
             case 160: return launch_tc<KIND, 160>(g, stream);
-            default: return launch_tc<KIND, 128>(g, stream);
+            case 128: return launch_tc<KIND, 128>(g, stream);
+            case 96: return launch_tc<KIND, 96>(g, stream);
+            default: return launch_tc<KIND, 64>(g, stream);
         }
     }
     dim3 grid((unsigned)((g.N + 63) / 64), (unsigned)((g.M + 63) / 64));

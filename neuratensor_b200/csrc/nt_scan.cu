@@ -644,6 +644,8 @@ int launch_selective_scan(int dtype, int state_dtype, const ScanArgs& a, cudaStr
 // Segments are consecutive row ranges of one sequence, so a (row, segment)
 // pair is handled as a "batch row" of length T/S at rows (b*S + s)*T/S.
 // ---------------------------------------------------------------------------
+constexpr int kMaxSegments = 8;   // scan_segments keeps B*S <= 8
+
 __global__ void __launch_bounds__(256) scan_seg_combine_kernel(int64_t B, int S, int64_t dN, const float* h_end,
                                                               const float* decay, const void* state_in, int sin_bf16,
                                                               float* h_in, void* state_out, int sout_bf16) {
@@ -652,10 +654,22 @@ __global__ void __launch_bounds__(256) scan_seg_combine_kernel(int64_t B, int S,
         float h = 0.f;
         if (state_in) h = sin_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(state_in)[i])
                                    : static_cast<const float*>(state_in)[i];
-        for (int s = 0; s < S; ++s) {
-            const int64_t v = (b * S + s) * dN + j;
-            h_in[v] = h;
-            h = fmaf(decay[v], h, h_end[v]);
+        // all segments' loads first (S <= kMaxSegments), then the chain
+        float e[kMaxSegments], q[kMaxSegments];
+#pragma unroll
+        for (int s = 0; s < kMaxSegments; ++s) {
+            if (s < S) {
+                const int64_t v = (b * S + s) * dN + j;
+                e[s] = h_end[v];
+                q[s] = decay[v];
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < kMaxSegments; ++s) {
+            if (s < S) {
+                h_in[(b * S + s) * dN + j] = h;
+                h = fmaf(q[s], h, e[s]);
+            }
         }
         if (state_out) {
             if (sout_bf16) static_cast<__nv_bfloat16*>(state_out)[i] = __float2bfloat16_rn(h);

@@ -155,3 +155,34 @@ def test_engine_api(small_bf16):
     assert out.shape == (1, 9)
     out = eng.generate(torch.randint(0, 1000, (1, 4)), max_new_tokens=30, top_k=1, stop_tokens=[0])
     assert out.shape[1] <= 34
+
+
+def test_generate_decode_graph_matches_eager():
+    """The captured single-token step gives the same logits and carried states
+    as running the step launch by launch (teacher-forced tokens), and
+    generate() returns the same tokens either way (with top_k=1 ties in the bf16
+    logits are broken by sampling, so both runs start from the same seed)."""
+    from neuratensor_b200 import ModelConfig, NeuraTensorModel
+    torch.manual_seed(5)
+    cfg = ModelConfig(vocab_size=1000, d_model=128, n_layers=4, d_state=16, max_seq_len=256, attn_every=2,
+                      attn_heads=2, attn_window=32)
+    model = NeuraTensorModel(cfg).to(DEV).to(torch.bfloat16).eval()
+    ids = torch.randint(0, 1000, (2, 16), device=DEV)
+    toks = torch.randint(0, 1000, (2, 24), device=DEV)
+    with torch.no_grad():
+        _, states, _ = model.forward_device(ids)
+        graph = model.decode_graph(2, ids.device, torch.bfloat16)
+        graph.load_states(states)
+        st_e = states
+        for t in range(toks.shape[1]):
+            lg_e, st_e, _ = model.forward_device(toks[:, t:t + 1], st_e)
+            lg_g = graph.step(toks[:, t:t + 1])
+            assert torch.equal(lg_e[:, -1, :], lg_g), t
+        for a, b in zip(st_e, graph.states()):
+            assert torch.equal(a.membrane, b.membrane) and torch.equal(a.ssm_state, b.ssm_state)
+        outs = []
+        for g in (False, True, True):              # the last run reuses the captured graph
+            torch.manual_seed(7)
+            out, _ = model.generate(ids, max_new_tokens=40, top_k=1, use_graph=g)
+            outs.append(out)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])

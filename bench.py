@@ -63,9 +63,11 @@ class Clocks:
     def __init__(self, device_index: int):
         self.dev = device_index
         self.rows = []          # (sm_mhz, max_mhz, reason names)
+        self.error = None
         self._stop = threading.Event()
         self._thread = None
         self._proc = None
+        self._nv = None
 
     def _nvml_handle(self):
         import pynvml
@@ -78,21 +80,32 @@ class Clocks:
         except Exception:
             return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
 
-    def _run_nvml(self, nv, h):
-        bits = [(name, getattr(nv, const)) for name, const in self.REASONS]
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    def _sample(self):
+        nv, h, mx, bits = self._nv
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.rows.append((float(sm), float(mx), [n for n, bit in bits if r & bit]))
+
+    def _run_nvml(self):
         while not self._stop.is_set():
-            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-            r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-            self.rows.append((float(sm), float(mx), [n for n, bit in bits if r & bit]))
+            try:
+                self._sample()
+            except Exception as e:          # keep what was sampled; say why sampling stopped
+                self.error = f"nvml: {e}"
+                return
             self._stop.wait(0.01)
 
     def __enter__(self):
         try:
             nv, h = self._nvml_handle()
-            self._thread = threading.Thread(target=self._run_nvml, args=(nv, h), daemon=True)
+            bits = [(name, getattr(nv, const)) for name, const in self.REASONS]
+            self._nv = (nv, h, nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM), bits)
+            self._sample()                  # at least one reading at the start of the region
+            self._thread = threading.Thread(target=self._run_nvml, daemon=True)
             self._thread.start()
-        except Exception:
+        except Exception as e:
+            self.error = f"nvml: {e}"
+            self._nv = None
             fields = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
                       "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                       "clocks_event_reasons.sw_power_cap")
@@ -108,6 +121,10 @@ class Clocks:
         if self._thread is not None:
             self._stop.set()
             self._thread.join(timeout=5)
+            try:
+                self._sample()              # and one at its end
+            except Exception as e:
+                self.error = f"nvml: {e}"
         if self._proc is not None:
             self._proc.terminate()
             try:
@@ -126,7 +143,7 @@ class Clocks:
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "error": self.error}
         return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
                 "reasons": sorted({n for r in self.rows for n in r[2]}), "samples": len(self.rows)}
 

@@ -246,19 +246,28 @@ class NeuraTensorModel(nn.Module):
         return sum(p.numel() for p in self.parameters() if p.requires_grad)
 
     @torch.no_grad()
-    def decode_graph(self, batch: int, device, dtype):
-        """The captured single-token step for this batch size.  A graph holds raw
-        addresses, so it is rebuilt when a parameter changes (version or storage)
-        or an attention layer's RoPE tables were rebuilt."""
-        from ..inference.decode import DecodeGraph
+    def step_graph(self, batch: int, seq: int, device, dtype):
+        """The captured forward for this (batch, length) (``inference/decode.py``).
+        A graph holds raw addresses, so it is rebuilt when a parameter changes
+        (version or storage) or an attention layer's RoPE tables were rebuilt;
+        the four most recently used shapes are kept."""
+        from ..inference.decode import StepGraph
         sig = (tuple((p.data_ptr(), p._version) for p in self.parameters()),
                tuple((a.rope.cos_cached.data_ptr(), a.rope.sin_cached.data_ptr()) for a in self.attn_layers.values()))
-        key = (batch, str(device), dtype)
-        cache = self.__dict__.setdefault("_decode_graphs", {})
-        if key not in cache or cache[key][0] != sig:
-            cache.pop(key, None)
-            cache[key] = (sig, DecodeGraph(self, batch, torch.device(device), dtype))
-        return cache[key][1]
+        key = (batch, seq, str(device), dtype)
+        cache = self.__dict__.setdefault("_step_graphs", {})
+        hit = cache.pop(key, None)
+        if hit is None or hit[0] != sig:
+            hit = None
+            while len(cache) >= 4:
+                cache.pop(next(iter(cache)))
+            hit = (sig, StepGraph(self, batch, seq, torch.device(device), dtype))
+        cache[key] = hit                          # most recently used last
+        return hit[1]
+
+    def decode_graph(self, batch: int, device, dtype):
+        """The captured single-token step for this batch size."""
+        return self.step_graph(batch, 1, device, dtype)
 
     def generate(self, input_ids: Tensor, max_new_tokens: int = 50, temperature: float = 1.0, top_k: int = 50,
                  top_p: float = 1.0, repetition_penalty: float = 1.0, stop_tokens: Optional[List[int]] = None,

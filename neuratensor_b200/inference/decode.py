@@ -1,21 +1,21 @@
-"""One decode step of the whole model as a CUDA graph.
+"""The whole model forward as a replayable CUDA graph, for a fixed batch and length.
 
-Autoregressive generation (model.py:301-370) runs the model on one new token
-per step with the block states carried over.  At one token per step the work
-per kernel is tiny and the step is bound by launch latency and host
-overhead: ~10 launches per block plus attention and the lm_head.  This module
-captures that step once per batch size into a CUDA graph and replays it:
+A forward of the native path is ~10 launches per block plus attention and the
+lm_head.  When the per-launch work is small (decoding one token, or a small
+per-GPU batch) the host's launch work is exposed; a captured graph replays
+all of it with one call.  ``StepGraph`` captures ``forward_device`` once for
+a (batch, length) shape:
 
-* static inputs: the token ids [B, 1] and, per block, the membrane [B, d_inner]
-  and SSM state [B, d_inner, d_state] in the model dtype;
-* the captured region runs ``NeuraTensorModel.forward_device`` on them and
-  copies the new states back into the static state buffers, so replay k+1
-  continues from replay k;
-* static outputs: the last position's logits [B, vocab] and the per-layer
-  spike counts.
+* static inputs: the token ids [B, T] and, per block, the membrane
+  [B, d_inner] and SSM state [B, d_inner, d_state] in the model dtype (zero
+  buffers stand for "no state", which the kernels treat as zeros);
+* the captured region runs the forward on them and copies the new states back
+  into the static state buffers, so replay k+1 continues from replay k;
+* static outputs: the logits [B, T, vocab] and the per-layer spike counts.
 
-Sampling (temperature, top-k/top-p, repetition penalty) stays eager on the
-returned logits, exactly as in the uncaptured loop.
+The graph holds raw device addresses: it owns its workspace, and the model
+rebuilds it when a parameter changes or a RoPE table is rebuilt
+(``NeuraTensorModel.step_graph``).  Sampling stays eager on the logits.
 """
 from __future__ import annotations
 
@@ -27,19 +27,18 @@ from torch import Tensor
 from ..core.fused import BlockState
 
 
-class DecodeGraph:
-    """A captured single-token step for one batch size, device and dtype."""
+class StepGraph:
+    """A captured forward for one (batch, length), device and dtype."""
 
-    def __init__(self, model, batch: int, device: torch.device, dtype: torch.dtype) -> None:
+    def __init__(self, model, batch: int, seq: int, device: torch.device, dtype: torch.dtype) -> None:
+        from .. import native
         cfg = model.config
         di = cfg.d_model * cfg.expand
         self.model = model
-        self.batch = batch
-        self.tok = torch.zeros((batch, 1), dtype=torch.int64, device=device)
+        self.tok = torch.zeros((batch, seq), dtype=torch.int64, device=device)
         self.mem = [torch.zeros((batch, di), dtype=dtype, device=device) for _ in model.blocks]
         self.st = [torch.zeros((batch, di, cfg.d_state), dtype=dtype, device=device) for _ in model.blocks]
-        from .. import native
-        nbytes = native.block_workspace_bytes(dtype, batch, 1, cfg.d_model, di, cfg.d_state)
+        nbytes = native.block_workspace_bytes(dtype, batch, seq, cfg.d_model, di, cfg.d_state)
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=device)   # owned: the graph keeps its address
         self.logits: Optional[Tensor] = None
         self.counts: Optional[Tensor] = None
@@ -49,27 +48,30 @@ class DecodeGraph:
     def _states(self) -> List[BlockState]:
         return [BlockState(membrane=m, ssm_state=s) for m, s in zip(self.mem, self.st)]
 
-    def _step(self):
+    def _forward(self):
         logits, new_states, counts = self.model.forward_device(self.tok, self._states(), workspace=self.ws)
         for i, ns in enumerate(new_states):
             self.mem[i].copy_(ns.membrane)
             self.st[i].copy_(ns.ssm_state)
-        return logits[:, -1, :], counts
+        return logits, counts
 
     def _capture(self) -> None:
-        side = torch.cuda.Stream(device=self.tok.device)
-        side.wait_stream(torch.cuda.current_stream(self.tok.device))
+        dev = self.tok.device
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side), torch.no_grad():
-            # warm-up outside the capture: builds weight caches, the workspace, the
-            # RoPE tables and each kernel's one-time attributes
+            # warm-up outside the capture: weight caches, RoPE tables and each
+            # kernel's one-time attributes are set up here
             for _ in range(2):
-                self._step()
-        torch.cuda.current_stream(self.tok.device).wait_stream(side)
+                self._forward()
+        torch.cuda.current_stream(dev).wait_stream(side)
         with torch.no_grad(), torch.cuda.graph(self.graph):
-            self.logits, self.counts = self._step()
+            self.logits, self.counts = self._forward()
 
-    def load_states(self, states: List[Optional[BlockState]]) -> None:
-        for i, s in enumerate(states):
+    def load_states(self, states: Optional[List[Optional[BlockState]]]) -> None:
+        """Start the next replay from `states` (None, or None entries: zero state)."""
+        for i in range(len(self.mem)):
+            s = None if states is None else states[i]
             if s is None:
                 self.mem[i].zero_()
                 self.st[i].zero_()
@@ -77,12 +79,16 @@ class DecodeGraph:
                 self.mem[i].copy_(s.membrane)
                 self.st[i].copy_(s.ssm_state)
 
-    def step(self, tok: Tensor) -> Tensor:
-        """Advance every sequence by the token ids `tok` [B, 1]; returns the logits [B, vocab]."""
-        self.tok.copy_(tok)
+    def replay(self, tok: Tensor) -> Tensor:
+        """Run the captured forward on token ids `tok` [B, T]; returns the static logits."""
+        self.tok.copy_(tok, non_blocking=True)
         self.graph.replay()
         return self.logits
 
+    def step(self, tok: Tensor) -> Tensor:
+        """Decode step (T = 1): the logits [B, vocab] of the new token."""
+        return self.replay(tok)[:, -1, :]
+
     def states(self) -> List[BlockState]:
-        """Copies of the carried states (the static buffers change on the next step)."""
+        """Copies of the carried states (the static buffers change on the next replay)."""
         return [BlockState(membrane=m.clone(), ssm_state=s.clone()) for m, s in zip(self.mem, self.st)]

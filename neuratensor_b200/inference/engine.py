@@ -59,6 +59,9 @@ class InferenceEngine:
             raise RuntimeError("neuratensor_b200 runs on CUDA (sm_100) only; got device=" + self.device)
         self.dtype = dtype or _best_dtype(self.device)
         self._states: List[Optional[BlockState]] = [None] * len(model.blocks)
+        # run() replays one captured CUDA graph per input shape (see inference/decode.py);
+        # False launches the kernels one by one (same kernels, same results)
+        self.use_graphs = True
         model = model.to(self.device).to(self.dtype)
         model.eval()
         self.model = model
@@ -108,12 +111,26 @@ class InferenceEngine:
         torch.cuda.synchronize(self.device)
         t0 = time.perf_counter()
         with torch.autocast(device_type="cuda", dtype=self.dtype, enabled=self.dtype != torch.float32):
-            logits, new_states, metrics = self.model(ids, self._states)
+            if self.use_graphs and ids.is_cuda:
+                logits, new_states, metrics = self._run_graph(ids)
+            else:
+                logits, new_states, metrics = self.model(ids, self._states)
         torch.cuda.synchronize(self.device)
         latency_ms = (time.perf_counter() - t0) * 1000.0
         self._states = new_states
         return InferenceResult(logits=logits, states=new_states, latency_ms=latency_ms, metrics=metrics,
                                device=self.device)
+
+    def _run_graph(self, ids: Tensor):
+        """The forward as one replay of the captured graph for this shape; the
+        logits and states returned are copies (the graph reuses its buffers)."""
+        B, T = ids.shape
+        g = self.model.step_graph(B, T, ids.device, self.dtype)
+        g.load_states(self._states)
+        logits = g.replay(ids).clone()
+        di = self.model.config.d_model * self.model.config.expand
+        metrics = self.model.metrics_from_counts(g.counts.tolist(), B * T * di, logits.dtype)
+        return logits, g.states(), metrics
 
     @torch.no_grad()
     def generate(self, input_ids: Tensor, max_new_tokens: int = 64, temperature: float = 1.0, top_k: int = 50,

@@ -186,3 +186,22 @@ def test_generate_decode_graph_matches_eager():
             out, _ = model.generate(ids, max_new_tokens=40, top_k=1, use_graph=g)
             outs.append(out)
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+def test_engine_run_graph_matches_eager(small_bf16):
+    """InferenceEngine.run replaying the captured forward equals the launch-by-launch
+    forward: logits, states and metrics, with and without carried state."""
+    eng, _ = small_bf16
+    ids = torch.randint(0, 32000, (2, 256))
+    runs = {}
+    for g in (False, True):
+        eng.use_graphs = g
+        r1 = eng.run(ids, reset_state=True)
+        r2 = eng.run(ids)                          # continues from r1's states
+        runs[g] = (r1, r2)
+    eng.use_graphs = True
+    for a, b in zip(runs[False], runs[True]):
+        assert torch.equal(a.logits, b.logits)
+        assert a.metrics["per_layer_spike_rate"] == b.metrics["per_layer_spike_rate"]
+        for sa, sb in zip(a.states, b.states):
+            assert torch.equal(sa.membrane, sb.membrane) and torch.equal(sa.ssm_state, sb.ssm_state)

@@ -211,7 +211,7 @@ def run_reference(args):
     cores = os.cpu_count() or 1
     line = {"metric": "tokens/s", "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": "small preset bf16 prefill (sampled: B=1 x T=64 per step on host cores)",
                        "preset": PRESET, "seq_len_sample": T_sample},

@@ -101,11 +101,11 @@ SsmWs ssm_ws(void* ws, int dtype, int64_t M, int64_t d, int64_t N) {
     return w;
 }
 
-struct SparseWs { unsigned char* flags; int* pos; int* idx; int* counters; void* oc; int64_t bytes; };
+struct SparseWs { unsigned* words; int* pos; int* idx; int* counters; void* oc; int64_t bytes; };
 SparseWs sparse_ws(void* ws, int dtype, int64_t M, int64_t K) {
     Carve c(ws);
     SparseWs w;
-    w.flags = c.take<unsigned char>(M);
+    w.words = c.take<unsigned>(4 * ((M + 31) / 32));
     w.pos = c.take<int>(M * 4);
     w.idx = c.take<int>(M * 4);
     w.counters = c.take<int>(64);
@@ -269,8 +269,8 @@ int nt_sparse_out_proj(int dtype, int64_t M, int64_t K, int64_t Nout, const void
     NT_TRY(check_gemm_operand(W, K, dtype, "nt_sparse_out_proj(W)"));
     if ((K * esize(dtype)) % 16) return fail(NT_ERR_ARG, "nt_sparse_out_proj: row bytes must be a multiple of 16");
     cudaStream_t st = as_stream(stream);
-    NT_TRY(launch_row_any(dtype, M, K, spikes, w.flags, st));
-    NT_TRY(launch_compact_rows(M, w.flags, w.pos, w.idx, w.counters, n_active_out, 1, st));
+    NT_TRY(launch_row_any_words(dtype, M, K, spikes, w.words, st));
+    NT_TRY(launch_compact_row_bits(1, M, 1, w.words, w.pos, w.idx, w.counters, 1, st, n_active_out));
     NT_TRY(launch_gather_rows(dtype, M, K, o, w.idx, w.counters, w.oc, st));
     GemmArgs g{};
     g.M = M; g.N = Nout; g.K = K;

@@ -59,22 +59,21 @@ int launch_lif_ssm_fused(const FusedArgs& a, cudaStream_t stream);
 int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w, void* y,
                    cudaStream_t stream);
 
-// Row activity: flags[r] = any(spikes[r, :] != 0) for a dense [M,K] matrix.
-int launch_row_any(int dtype, int64_t M, int64_t K, const void* spikes, unsigned char* flags,
-                   cudaStream_t stream);
-// Exclusive scan of flags -> counters[0] = n_active, counters[1] = 1 when the
-// sparse branch is taken (2*n_active <= M), counters[2] = rows the out_proj
-// GEMM processes.  Only on the sparse branch are row_pos (position among
-// active rows, or -1) and row_idx (inverse map, first n_active entries)
-// written; consumers treat both as the identity when counters[1] == 0.
-// n_active_out (optional) receives n_active as int64.
-int launch_compact_rows(int64_t M, const unsigned char* flags, int* row_pos, int* row_idx,
-                        int* counters, long long* n_active_out, int sparse_enabled,
-                        cudaStream_t stream);
-// The same decision and maps from the LIF's row-activity bits (M = B*T rows,
-// n_cblk channel blocks, layout of LifArgs::row_bits).
+// Row compaction (the density decision of _sparse_out_proj): counters[0] =
+// n_active, counters[1] = 1 when the sparse branch is taken (2*n_active <= M),
+// counters[2] = rows the out_proj GEMM processes.  Only on the sparse branch
+// are row_pos (position among active rows, or -1) and row_idx (inverse map,
+// first n_active entries) written; consumers treat both as the identity when
+// counters[1] == 0.  n_active_out (optional) receives n_active as int64.
+// Input: row-activity bits (M = B*T rows, n_cblk channel blocks, the layout of
+// LifArgs::row_bits).
 int launch_compact_row_bits(int64_t B, int64_t T, int64_t n_cblk, const unsigned* row_bits, int* row_pos,
-                            int* row_idx, int* counters, int sparse_enabled, cudaStream_t stream);
+                            int* row_idx, int* counters, int sparse_enabled, cudaStream_t stream,
+                            long long* n_active_out = nullptr);
+// Row activity of a dense [M,K] matrix as 32-row words (bit j of words[g]: row 32g + j
+// has a non-zero value); the layout of launch_compact_row_bits with B = 1, n_cblk = 1.
+int launch_row_any_words(int dtype, int64_t M, int64_t K, const void* spikes, unsigned* words,
+                         cudaStream_t stream);
 // Gather active rows of src [M,K] into dst [n_active,K] (dst row i = src row row_idx[i];
 // every row, in order, when counters[1] == 0).
 int launch_gather_rows(int dtype, int64_t M, int64_t K, const void* src, const int* row_idx,

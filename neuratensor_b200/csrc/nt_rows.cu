@@ -59,40 +59,56 @@ int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w
 // flags[r] = any(spikes[r, :] != 0).  One warp per row, 16-byte loads when
 // the row is 16-byte aligned; a value is non-zero when its magnitude bits
 // are (so -0.0 counts as zero, as in torch's `any`).
-// ---------------------------------------------------------------------------
+// Row activity as 32-row words: bit j of words[g] is set when row 32g + j has
+// a non-zero value.  A 256-thread block owns one word; each warp tests four
+// rows (16-byte loads when rows are 16-byte aligned), then warp 0 packs the
+// 32 answers with a ballot.
 template <int DT>
-__global__ void __launch_bounds__(256) row_any_kernel(int64_t M, int64_t K, const void* sv, unsigned char* flags) {
+__global__ void __launch_bounds__(256) row_any_words_kernel(int64_t M, int64_t K, const void* sv, unsigned* words) {
     using T = typename Elem<DT>::T;
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    __shared__ int any_row[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t row_bytes = K * (int64_t)sizeof(T);
     const bool vec = (row_bytes % 16 == 0) && ((reinterpret_cast<uintptr_t>(sv) & 15) == 0);
     const uint32_t mag = sizeof(T) == 2 ? 0x7FFF7FFFu : 0x7FFFFFFFu;
-    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
-        uint32_t acc = 0;
-        if (vec) {
-            const uint4* p = reinterpret_cast<const uint4*>(static_cast<const char*>(sv) + r * row_bytes);
-            const int64_t nv = row_bytes / 16;
-            for (int64_t i = lane; i < nv; i += 32) {
-                const uint4 q = __ldg(p + i);
-                acc |= (q.x | q.y | q.z | q.w) & mag;
+    const int64_t n_words = (M + 31) / 32;
+    for (int64_t g = blockIdx.x; g < n_words; g += gridDim.x) {
+#pragma unroll 1
+        for (int j = warp; j < 32; j += 8) {
+            const int64_t r = 32 * g + j;
+            uint32_t acc = 0;
+            if (r < M) {
+                if (vec) {
+                    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const char*>(sv) + r * row_bytes);
+                    for (int64_t i = lane; i < row_bytes / 16; i += 32) {
+                        const uint4 q = __ldg(p + i);
+                        acc |= (q.x | q.y | q.z | q.w) & mag;
+                    }
+                } else {
+                    const T* p = static_cast<const T*>(sv) + r * K;
+                    for (int64_t i = lane; i < K; i += 32) acc |= (Elem<DT>::load(p + i) != 0.f) ? 1u : 0u;
+                }
             }
-        } else {
-            const T* p = static_cast<const T*>(sv) + r * K;
-            for (int64_t i = lane; i < K; i += 32) acc |= (Elem<DT>::load(p + i) != 0.f) ? 1u : 0u;
+            const unsigned a = __ballot_sync(0xffffffffu, acc != 0);
+            if (lane == 0) any_row[j] = a != 0;
         }
-        const unsigned any = __ballot_sync(0xffffffffu, acc != 0);
-        if (lane == 0) flags[r] = any ? 1 : 0;
+        __syncthreads();
+        if (warp == 0) {
+            const unsigned w = __ballot_sync(0xffffffffu, any_row[lane] != 0);
+            if (lane == 0) words[g] = w;
+        }
+        __syncthreads();
     }
 }
 
-int launch_row_any(int dtype, int64_t M, int64_t K, const void* spikes, unsigned char* flags, cudaStream_t stream) {
-    const int64_t blocks = std::min<int64_t>((M + 7) / 8, 148 * 16);
-    if (dtype == NT_F32) row_any_kernel<NT_F32><<<(unsigned)blocks, 256, 0, stream>>>(M, K, spikes, flags);
-    else if (dtype == NT_BF16) row_any_kernel<NT_BF16><<<(unsigned)blocks, 256, 0, stream>>>(M, K, spikes, flags);
+int launch_row_any_words(int dtype, int64_t M, int64_t K, const void* spikes, unsigned* words, cudaStream_t stream) {
+    const int64_t blocks = std::min<int64_t>((M + 31) / 32, 148 * 16);
+    if (dtype == NT_F32) row_any_words_kernel<NT_F32><<<(unsigned)blocks, 256, 0, stream>>>(M, K, spikes, words);
+    else if (dtype == NT_BF16) row_any_words_kernel<NT_BF16><<<(unsigned)blocks, 256, 0, stream>>>(M, K, spikes, words);
     else return fail(NT_ERR_DTYPE, "row_any: dtype %d", dtype);
-    return check_launch("row_any_kernel");
+    return check_launch("row_any_words_kernel");
 }
+
 
 // ---------------------------------------------------------------------------
 // Single-CTA stream compaction.  counters[0] = n_active, counters[1] = 1 when
@@ -125,47 +141,13 @@ __device__ __forceinline__ int cta_scan_1024(int v, int* warp_tot, int* total) {
     __syncthreads();
     return v + (warp ? warp_tot[warp - 1] : 0);
 }
-__global__ void __launch_bounds__(1024) compact_rows_kernel(int64_t M, const unsigned char* flags, int* row_pos,
-                                                            int* row_idx, int* counters, long long* n_active_out,
-                                                            int sparse_enabled) {
-    __shared__ int warp_tot[32];
-    __shared__ int s_total;
-    const int tid = threadIdx.x;
-    const int64_t per = (M + 1023) / 1024;
-    const int64_t r0 = tid * per, r1 = (r0 + per < M) ? r0 + per : M;
-    int cnt = 0;
-    for (int64_t r = r0; r < r1; ++r) cnt += flags[r] ? 1 : 0;
-    const int incl = cta_scan_1024(cnt, warp_tot, &s_total);
-    const int n_active = s_total;
-    const bool sparse = sparse_enabled && (2LL * n_active <= M);
-    int pos = incl - cnt;                                  // exclusive prefix
-    if (sparse) {
-        for (int64_t r = r0; r < r1; ++r) {
-            if (flags[r]) { row_pos[r] = pos; row_idx[pos] = (int)r; ++pos; }
-            else row_pos[r] = -1;
-        }
-    }
-    if (tid == 0) {
-        counters[0] = n_active;
-        counters[1] = sparse ? 1 : 0;
-        counters[2] = sparse ? n_active : (int)M;
-        if (n_active_out) *n_active_out = n_active;
-    }
-}
-
-int launch_compact_rows(int64_t M, const unsigned char* flags, int* row_pos, int* row_idx, int* counters,
-                        long long* n_active_out, int sparse_enabled, cudaStream_t stream) {
-    if (M > (int64_t)INT32_MAX) return fail(NT_ERR_ARG, "compact_rows: M too large");
-    compact_rows_kernel<<<1, 1024, 0, stream>>>(M, flags, row_pos, row_idx, counters, n_active_out, sparse_enabled);
-    return check_launch("compact_rows_kernel");
-}
-
 // The same from row-activity words: word (b, w) covers rows b*T + 32w + j,
 // j < min(32, T - 32w); a row is active when any channel block set its bit.
 // Thread i owns a run of consecutive words.
 __global__ void __launch_bounds__(1024) compact_row_bits_kernel(int64_t B, int64_t T, int64_t n_cblk,
                                                                 const unsigned* bits, int* row_pos, int* row_idx,
-                                                                int* counters, int sparse_enabled) {
+                                                                int* counters, int sparse_enabled,
+                                                                long long* n_active_out) {
     __shared__ int warp_tot[32];
     __shared__ int s_total;
     const int64_t n_words = (T + 31) / 32, words = B * n_words;
@@ -201,14 +183,16 @@ __global__ void __launch_bounds__(1024) compact_row_bits_kernel(int64_t B, int64
         counters[0] = n_active;
         counters[1] = sparse ? 1 : 0;
         counters[2] = sparse ? n_active : (int)M;
+        if (n_active_out) *n_active_out = n_active;
     }
 }
 
 int launch_compact_row_bits(int64_t B, int64_t T, int64_t n_cblk, const unsigned* row_bits, int* row_pos,
-                            int* row_idx, int* counters, int sparse_enabled, cudaStream_t stream) {
+                            int* row_idx, int* counters, int sparse_enabled, cudaStream_t stream,
+                            long long* n_active_out) {
     if (B * T > (int64_t)INT32_MAX) return fail(NT_ERR_ARG, "compact_row_bits: B*T too large");
     compact_row_bits_kernel<<<1, 1024, 0, stream>>>(B, T, n_cblk, row_bits, row_pos, row_idx, counters,
-                                                    sparse_enabled);
+                                                    sparse_enabled, n_active_out);
     return check_launch("compact_row_bits_kernel");
 }
 
@@ -238,28 +222,39 @@ int launch_gather_rows(int dtype, int64_t M, int64_t K, const void* src, const i
 }
 
 // For rows skipped by the sparse branch (row_pos[r] < 0 and counters[1] != 0):
-// dst[r, :] = src ? src[r, :] : 0.
+// dst[r, :] = src ? src[r, :] : 0.  One warp per row; active rows are skipped
+// whole; 16-byte accesses when the rows allow them.
 template <typename T>
 __global__ void __launch_bounds__(256) fill_inactive_kernel(int64_t M, int64_t N, const int* row_pos,
-                                                            const int* counters, const T* src, T* dst) {
+                                                            const int* counters, const T* src, T* dst, int vec) {
     if (counters[1] == 0) return;
-    const int64_t total = M * N;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / N;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
         if (row_pos[r] >= 0) continue;
-        dst[i] = src ? src[i] : T(0.f);
+        if (vec) {
+            constexpr int EPV = 16 / (int)sizeof(T);
+            uint4* d = reinterpret_cast<uint4*>(dst + r * N);
+            const uint4* sp = src ? reinterpret_cast<const uint4*>(src + r * N) : nullptr;
+            for (int64_t i = lane; i < N / EPV; i += 32) d[i] = sp ? __ldg(sp + i) : make_uint4(0, 0, 0, 0);
+        } else {
+            for (int64_t i = lane; i < N; i += 32) dst[r * N + i] = src ? src[r * N + i] : T(0.f);
+        }
     }
 }
 
 int launch_fill_inactive(int dtype, int64_t M, int64_t N, const int* row_pos, const int* counters,
                          const void* src, void* dst, cudaStream_t stream) {
-    const int64_t blocks = std::min<int64_t>((M * N + 255) / 256, 148 * 16);
+    const int64_t es = dtype == NT_F32 ? 4 : 2;
+    const int vec = (N * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+    const int64_t blocks = std::max<int64_t>(std::min<int64_t>((M + 7) / 8, 148 * 16), 1);
     if (dtype == NT_F32)
-        fill_inactive_kernel<float><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
-            M, N, row_pos, counters, static_cast<const float*>(src), static_cast<float*>(dst));
+        fill_inactive_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(
+            M, N, row_pos, counters, static_cast<const float*>(src), static_cast<float*>(dst), vec);
     else
-        fill_inactive_kernel<__nv_bfloat16><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
-            M, N, row_pos, counters, static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst));
+        fill_inactive_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(
+            M, N, row_pos, counters, static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst), vec);
     return check_launch("fill_inactive_kernel");
 }
 

@@ -36,8 +36,15 @@ class StepGraph:
         di = cfg.d_model * cfg.expand
         self.model = model
         self.tok = torch.zeros((batch, seq), dtype=torch.int64, device=device)
-        self.mem = [torch.zeros((batch, di), dtype=dtype, device=device) for _ in model.blocks]
-        self.st = [torch.zeros((batch, di, cfg.d_state), dtype=dtype, device=device) for _ in model.blocks]
+        # every block's membrane and SSM state as views of one flat buffer (one memset,
+        # one copy for all of them)
+        n_mem, n_st = batch * di, batch * di * cfg.d_state
+        self.flat = torch.zeros(len(model.blocks) * (n_mem + n_st), dtype=dtype, device=device)
+        self._split = lambda buf: (
+            [buf[i * (n_mem + n_st):i * (n_mem + n_st) + n_mem].view(batch, di) for i in range(len(model.blocks))],
+            [buf[i * (n_mem + n_st) + n_mem:(i + 1) * (n_mem + n_st)].view(batch, di, cfg.d_state)
+             for i in range(len(model.blocks))])
+        self.mem, self.st = self._split(self.flat)
         nbytes = native.block_workspace_bytes(dtype, batch, seq, cfg.d_model, di, cfg.d_state)
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=device)   # owned: the graph keeps its address
         self.logits: Optional[Tensor] = None
@@ -70,8 +77,11 @@ class StepGraph:
 
     def load_states(self, states: Optional[List[Optional[BlockState]]]) -> None:
         """Start the next replay from `states` (None, or None entries: zero state)."""
+        if states is None or all(s is None for s in states):
+            self.flat.zero_()
+            return
         for i in range(len(self.mem)):
-            s = None if states is None else states[i]
+            s = states[i]
             if s is None:
                 self.mem[i].zero_()
                 self.st[i].zero_()
@@ -91,4 +101,5 @@ class StepGraph:
 
     def states(self) -> List[BlockState]:
         """Copies of the carried states (the static buffers change on the next replay)."""
-        return [BlockState(membrane=m.clone(), ssm_state=s.clone()) for m, s in zip(self.mem, self.st)]
+        mem, st = self._split(self.flat.clone())
+        return [BlockState(membrane=m, ssm_state=s) for m, s in zip(mem, st)]

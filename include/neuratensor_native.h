@@ -192,10 +192,11 @@ NT_API int nt_lif_ssm_fused(int64_t B, int64_t L, int64_t d, int64_t N,
  * SlidingWindowAttention.forward (model.py:159-178: q/k/v from the qkv
  * projection, apply_rotary on q and k (model.py:119-126), then
  * scaled_dot_product_attention with the causal window mask j in [i-window, i]).
- * bf16 only, head_dim 64.  qkv: [B*T, ld_qkv] rows, columns [q | k | v] of
- * n_heads*64 each; cos_t, sin_t: [T, 64] bf16 rotary tables (the module's
- * cached ones); out: [B*T, ld_out], head h in columns h*64 .. h*64+63 (the
- * transpose(1,2).reshape layout o_proj takes).  Softmax scale 1/8.  RoPE
+ * bf16 only, head_dim (HD) 64 or 128.  qkv: [B*T, ld_qkv] rows, columns
+ * [q | k | v] of n_heads*HD each; cos_t, sin_t: [T, HD] bf16 rotary tables
+ * (the module's cached ones); out: [B*T, ld_out], head h in columns
+ * h*HD .. h*HD+HD-1 (the transpose(1,2).reshape layout o_proj takes).
+ * Softmax scale 1/sqrt(HD).  RoPE
  * rounds like the reference's bf16 ops; scores and softmax in float32, the
  * probabilities rounded to bf16 before the product with v. */
 NT_API int nt_window_attention(int dtype, int64_t B, int64_t T, int64_t n_heads, int64_t head_dim,

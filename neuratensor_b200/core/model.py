@@ -123,7 +123,7 @@ class SlidingWindowAttention(nn.Module):
         return self._mask
 
     def forward(self, x: Tensor) -> Tensor:
-        if x.is_cuda and x.dtype == torch.bfloat16 and self.head_dim == 64:
+        if x.is_cuda and x.dtype == torch.bfloat16 and self.head_dim in (64, 128):
             return self.forward_native(x)
         return self.forward_torch(x)
 
@@ -138,7 +138,7 @@ class SlidingWindowAttention(nn.Module):
         return self.o_proj(o) + x
 
     def forward_torch(self, x: Tensor) -> Tensor:
-        """The reference's op sequence (fp32, CPU tensors, head dims other than 64)."""
+        """The reference's op sequence (fp32, CPU tensors, head dims other than 64 and 128)."""
         B, T, _ = x.shape
         h = self.norm(x)
         q, k, v = self.qkv(h).view(B, T, 3, self.n_heads, self.head_dim).permute(2, 0, 3, 1, 4).unbind(0)
@@ -201,9 +201,25 @@ class NeuraTensorModel(nn.Module):
             self._ws = torch.empty(n, dtype=torch.uint8, device=x.device)
         return self._ws
 
+    # The kernels index activations with 32-bit element offsets in places; a
+    # forward whose widest activation (the in_proj output [rows, 2*d_inner] or
+    # attention's qkv [rows, 3*d_model]) would pass 2^30 elements runs the
+    # batch in groups of sequences instead (sequences are independent, so
+    # the result is the same).
+    MAX_ACTIVATION_ELEMS = 1 << 30
+
+    def group_size(self, seq: int) -> int:
+        """Sequences of length `seq` that one pass of the blocks takes at most."""
+        c = self.config
+        width = max(2 * c.d_model * c.expand, 3 * c.d_model)
+        return max(1, self.MAX_ACTIVATION_ELEMS // (max(seq, 1) * width))
+
     def forward_device(self, input_ids: Tensor, states: Optional[List[Optional[BlockState]]] = None,
-                       workspace: Optional[Tensor] = None):
-        """Forward without any host sync: returns (logits, states, per-layer spike counts on device)."""
+                       workspace: Optional[Tensor] = None, last_only: bool = False):
+        """Forward without any host sync: returns (logits, states, per-layer spike counts on device).
+
+        ``last_only``: logits of the last position only ([B, 1, vocab]), as a
+        generation prefill needs them."""
         if states is None:
             states = [None] * len(self.blocks)
         if input_ids.shape[1] > self.config.max_seq_len:
@@ -211,6 +227,24 @@ class NeuraTensorModel(nn.Module):
             warnings.warn(f"Input sequence length {input_ids.shape[1]} exceeds max_seq_len "
                           f"{self.config.max_seq_len}; truncating.", UserWarning, stacklevel=3)
             input_ids = input_ids[:, : self.config.max_seq_len]
+        B, T = input_ids.shape
+        g = self.group_size(T)
+        if B <= g:
+            return self._forward_rows(input_ids, states, workspace, last_only)
+        parts = []
+        for a in range(0, B, g):
+            sub = [None if s is None else BlockState(membrane=s.membrane[a:a + g], ssm_state=s.ssm_state[a:a + g])
+                   for s in states]
+            parts.append(self._forward_rows(input_ids[a:a + g], sub, workspace, last_only))
+        logits = torch.cat([p[0] for p in parts])
+        new_states = [BlockState(membrane=torch.cat([p[1][i].membrane for p in parts]),
+                                 ssm_state=torch.cat([p[1][i].ssm_state for p in parts]))
+                      for i in range(len(self.blocks))]
+        counts = torch.stack([p[2] for p in parts]).sum(0)
+        return logits, new_states, counts
+
+    def _forward_rows(self, input_ids: Tensor, states: List[Optional[BlockState]], workspace: Optional[Tensor],
+                      last_only: bool):
         x = self.embedding(input_ids)
         counts = torch.zeros(len(self.blocks), dtype=torch.int64, device=x.device)
         ws = workspace if workspace is not None else self._workspace(x)
@@ -222,6 +256,8 @@ class NeuraTensorModel(nn.Module):
                 key = str(i)
                 if key in self.attn_layers:
                     x = self.attn_layers[key](x)
+            if last_only:
+                x = x[:, -1:]
             logits = self.lm_head(self.norm(x))
         return logits, new_states, counts
 
@@ -281,7 +317,7 @@ class NeuraTensorModel(nn.Module):
         self.eval()
         out = input_ids
         stop = set(stop_tokens or [])
-        logits, states, _ = self.forward_device(out, states)
+        logits, states, _ = self.forward_device(out, states, last_only=True)
         nxt_logits = logits[:, -1, :]
         graph = None
         if use_graph and out.is_cuda and max_new_tokens > 1:

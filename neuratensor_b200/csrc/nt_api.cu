@@ -396,16 +396,18 @@ int nt_window_attention(int dtype, int64_t B, int64_t T, int64_t n_heads, int64_
                         const void* qkv, int64_t ld_qkv, const void* cos_t, const void* sin_t, void* out,
                         int64_t ld_out, void* stream) {
     if (dtype != NT_BF16) return fail(NT_ERR_DTYPE, "nt_window_attention: bf16 only (dtype %d)", dtype);
-    if (head_dim != 64) return fail(NT_ERR_ARG, "nt_window_attention: head_dim %lld (64 supported)", (long long)head_dim);
+    if (head_dim != 64 && head_dim != 128)
+        return fail(NT_ERR_ARG, "nt_window_attention: head_dim %lld (64 or 128 supported)", (long long)head_dim);
     if (B < 1 || T < 1 || n_heads < 1 || window < 0 || B > 65535 || n_heads > 65535 || T > (int64_t)INT32_MAX / 2)
         return fail(NT_ERR_ARG, "nt_window_attention: bad sizes");
     if (!qkv || !cos_t || !sin_t || !out) return fail(NT_ERR_ARG, "nt_window_attention: null pointer");
-    if (ld_qkv < 3 * n_heads * 64 || ld_out < n_heads * 64)
+    if (ld_qkv < 3 * n_heads * head_dim || ld_out < n_heads * head_dim)
         return fail(NT_ERR_ARG, "nt_window_attention: leading dimensions too small");
     if (ld_qkv % 8 || ld_out % 2 || !aligned16(qkv) || !aligned16(cos_t) || !aligned16(sin_t) ||
         (reinterpret_cast<uintptr_t>(out) & 3))
         return fail(NT_ERR_ARG, "nt_window_attention: qkv/cos/sin need 16-byte aligned rows, out 4-byte");
-    return launch_window_attention(B, T, n_heads, window, qkv, ld_qkv, cos_t, sin_t, out, ld_out, as_stream(stream));
+    return launch_window_attention(B, T, n_heads, head_dim, window, qkv, ld_qkv, cos_t, sin_t, out, ld_out,
+                                   as_stream(stream));
 }
 
 int nt_lif_ssm_fused(int64_t B, int64_t L, int64_t d, int64_t N, const void* x, const void* delta, const void* Bm,

@@ -85,8 +85,9 @@ int launch_fill_inactive(int dtype, int64_t M, int64_t N, const int* row_pos, co
 // Sliding-window causal attention with RoPE, bf16, head_dim 64: qkv row-major
 // [B*T, ld_qkv] with columns [q | k | v] (H heads of 64 each), cos/sin [T][64]
 // bf16, out [B*T, ld_out] (head h in columns h*64 .. h*64+63).
-int launch_window_attention(int64_t B, int64_t T, int64_t H, int64_t window, const void* qkv, int64_t ld_qkv,
-                            const void* cos_t, const void* sin_t, void* out, int64_t ld_out, cudaStream_t stream);
+int launch_window_attention(int64_t B, int64_t T, int64_t H, int64_t head_dim, int64_t window, const void* qkv,
+                            int64_t ld_qkv, const void* cos_t, const void* sin_t, void* out, int64_t ld_out,
+                            cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // GEMM: D[M,N] = A[M,K] * B[N,K]^T with a fused epilogue.

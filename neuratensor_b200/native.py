@@ -332,9 +332,10 @@ def lif_ssm_fused(x: Tensor, delta: Tensor, Bm: Tensor, Cm: Tensor, log_A: Tenso
 def window_attention(qkv: Tensor, n_heads: int, window: int, cos: Tensor, sin: Tensor) -> Tensor:
     """RoPE + sliding-window causal SDPA of SlidingWindowAttention.forward (model.py:159-178).
 
-    qkv: [B, T, 3*d_model] bf16 (the qkv projection's output), cos/sin: [T, 64]
-    rotary tables; returns the attention output [B, T, d_model] (heads
-    concatenated, as o_proj takes it)."""
+    qkv: [B, T, 3*d_model] bf16 (the qkv projection's output), head_dim =
+    d_model / n_heads of 64 or 128; cos/sin: [T, head_dim] rotary tables;
+    returns the attention output [B, T, d_model] (heads concatenated, as
+    o_proj takes it)."""
     dev = _require_cuda(qkv, cos, sin)
     if qkv.dtype != torch.bfloat16:
         raise NativeError("nt_window_attention", 2, "bf16 only")
@@ -342,16 +343,17 @@ def window_attention(qkv: Tensor, n_heads: int, window: int, cos: Tensor, sin: T
         raise ValueError(f"qkv must be [B, T, 3*d_model], got {tuple(qkv.shape)}")
     B, T, three_dm = qkv.shape
     dm = three_dm // 3
-    if three_dm != 3 * dm or dm != 64 * n_heads:
-        raise ValueError(f"qkv width {three_dm} does not match {n_heads} heads of 64")
+    hd = dm // n_heads if n_heads > 0 else 0
+    if three_dm != 3 * dm or hd not in (64, 128) or dm != hd * n_heads:
+        raise ValueError(f"qkv width {three_dm} does not split into {n_heads} heads of 64 or 128")
     if qkv.stride(2) != 1 or qkv.stride(0) != T * qkv.stride(1):
         qkv = qkv.contiguous()
     cos = cos[:T].to(torch.bfloat16).contiguous()
     sin = sin[:T].to(torch.bfloat16).contiguous()
-    if cos.shape != (T, 64) or sin.shape != (T, 64):
-        raise ValueError("cos/sin must hold at least T rows of 64")
+    if cos.shape != (T, hd) or sin.shape != (T, hd):
+        raise ValueError(f"cos/sin must hold at least T rows of {hd}")
     out = torch.empty((B, T, dm), dtype=torch.bfloat16, device=dev)
-    rc = load().nt_window_attention(_dtype_code(qkv), B, T, n_heads, 64, int(window), _p(qkv), qkv.stride(1),
+    rc = load().nt_window_attention(_dtype_code(qkv), B, T, n_heads, hd, int(window), _p(qkv), qkv.stride(1),
                                     _p(cos), _p(sin), _p(out), out.stride(1), _stream(dev))
     _check("nt_window_attention", rc)
     return out

@@ -398,14 +398,17 @@ def test_block_forward_bf16_vs_oracle(nat, sparse_rows):
 #  Sliding-window attention (model.py:148-182)                                 #
 # --------------------------------------------------------------------------- #
 
-@pytest.mark.parametrize("B,T,heads,window", [(2, 300, 2, 256), (1, 100, 3, 256), (1, 1, 2, 256),
-                                              (2, 130, 2, 32), (1, 2048, 10, 256)])
-def test_window_attention_vs_reference_ops(nat, B, T, heads, window):
-    """Native RoPE + windowed SDPA against the reference's op sequence on the same module."""
+@pytest.mark.parametrize("B,T,heads,window,hd", [(2, 300, 2, 256, 64), (1, 100, 3, 256, 64), (1, 1, 2, 256, 64),
+                                                 (2, 130, 2, 32, 64), (1, 2048, 10, 256, 64),
+                                                 (2, 300, 2, 256, 128), (1, 1, 1, 512, 128),
+                                                 (1, 1100, 3, 512, 128), (1, 700, 16, 512, 128)])
+def test_window_attention_vs_reference_ops(nat, B, T, heads, window, hd):
+    """Native RoPE + windowed SDPA against the reference's op sequence on the
+    same module; head_dim 64 (small preset) and 128 (large preset)."""
     from neuratensor_b200.core.model import SlidingWindowAttention
     torch.manual_seed(11)
-    att = SlidingWindowAttention(64 * heads, n_heads=heads, window=window).to(DEV).to(torch.bfloat16).eval()
-    x = torch.randn(B, T, 64 * heads, device=DEV).to(torch.bfloat16)
+    att = SlidingWindowAttention(hd * heads, n_heads=heads, window=window).to(DEV).to(torch.bfloat16).eval()
+    x = torch.randn(B, T, hd * heads, device=DEV).to(torch.bfloat16)
     with torch.no_grad():
         ref = att.forward_torch(x).float()
         out = att.forward_native(x).float()
@@ -414,14 +417,15 @@ def test_window_attention_vs_reference_ops(nat, B, T, heads, window):
     assert diff.mean().item() < 4e-3, diff.mean().item()
 
 
-def test_window_attention_window_zero_is_v(nat):
+@pytest.mark.parametrize("hd", [64, 128])
+def test_window_attention_window_zero_is_v(nat, hd):
     """window 0: every query sees only its own key, so the output is v exactly."""
     B, T, H = 2, 70, 2
-    qkv = torch.randn(B, T, 3 * 64 * H, device=DEV).to(torch.bfloat16)
-    cos = torch.randn(T, 64, device=DEV).to(torch.bfloat16)
-    sin = torch.randn(T, 64, device=DEV).to(torch.bfloat16)
+    qkv = torch.randn(B, T, 3 * hd * H, device=DEV).to(torch.bfloat16)
+    cos = torch.randn(T, hd, device=DEV).to(torch.bfloat16)
+    sin = torch.randn(T, hd, device=DEV).to(torch.bfloat16)
     out = nat.window_attention(qkv, H, 0, cos, sin)
-    assert torch.equal(out, qkv[:, :, 2 * 64 * H:])
+    assert torch.equal(out, qkv[:, :, 2 * hd * H:])
 
 
 def test_window_attention_rejects_bad_args(nat):

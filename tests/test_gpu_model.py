@@ -205,3 +205,37 @@ def test_engine_run_graph_matches_eager(small_bf16):
         assert a.metrics["per_layer_spike_rate"] == b.metrics["per_layer_spike_rate"]
         for sa, sb in zip(a.states, b.states):
             assert torch.equal(sa.membrane, sb.membrane) and torch.equal(sa.ssm_state, sb.ssm_state)
+
+
+def test_forward_in_sequence_groups_matches_one_pass():
+    """A batch that passes the activation-size limit runs in groups of
+    sequences: same logits, carried states and spike counts as one pass, with
+    and without carry-in state; last_only gives the last position's logits.
+    head_dim 128 puts the attention on the 128-wide kernel."""
+    from neuratensor_b200 import ModelConfig, NeuraTensorModel
+    torch.manual_seed(6)
+    cfg = ModelConfig(vocab_size=1000, d_model=256, n_layers=3, d_state=32, max_seq_len=512, attn_every=3,
+                      attn_heads=2, attn_window=64)
+    model = NeuraTensorModel(cfg).to(DEV).to(torch.bfloat16).eval()
+    ids = torch.randint(0, 1000, (5, 200), device=DEV)
+    with torch.no_grad():
+        lg1, st1, c1 = model.forward_device(ids)
+        lg1b, st1b, c1b = model.forward_device(ids, st1)
+        model.MAX_ACTIVATION_ELEMS = 2 * 200 * 2 * 256 * 2          # two sequences per group
+        assert model.group_size(200) == 2
+        lg2, st2, c2 = model.forward_device(ids)
+        lg2b, st2b, c2b = model.forward_device(ids, st2)
+        last, _, _ = model.forward_device(ids, st2, last_only=True)
+        del model.MAX_ACTIVATION_ELEMS
+    # a GEMM library may pick another kernel for fewer rows, so values within
+    # bf16 tolerance (a mis-sliced group or state would be off by O(1))
+    close = lambda a, b: torch.testing.assert_close(a.float(), b.float(), rtol=2e-2, atol=2e-2)
+    for a, b in ((lg1, lg2), (lg1b, lg2b)):
+        close(a, b)
+    for a, b in ((c1, c2), (c1b, c2b)):
+        assert (a - b).abs().max().item() <= 0.01 * a.max().item() + 2
+    for s1, s2 in zip(st1 + st1b, st2 + st2b):
+        close(s1.membrane, s2.membrane)
+        close(s1.ssm_state, s2.ssm_state)
+    assert last.shape == (5, 1, 1000)
+    torch.testing.assert_close(last[:, 0].float(), lg2b[:, -1].float(), rtol=2e-2, atol=2e-2)

@@ -591,6 +591,134 @@ int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Short sequences (decode steps, T <= kStepMaxT): one warp per (batch row,
+// channel), lane l holding states l, l+32, ... in registers, with no shared
+// memory staging.  The chunked kernel above stages and steps through a whole
+// 16-32-step chunk and pays its per-CTA set-up for every 8-16 channels, which
+// for one step costs ~40x the step itself; this kernel is bounded by reading
+// and writing the state.  Same arithmetic as the chunked kernel (A rounded
+// like the reference's op, the HiPPO form h' = h + e (h + w) when log_A has the
+// HiPPO structure -- tested per channel here, per CTA there -- and the general
+// (A_bar - 1)/A form otherwise), but each state's exponential is taken
+// directly instead of by the chunked kernel's product chain, and C.h is summed
+// by a warp reduction: results agree with it to a few float32 ulps.
+constexpr int kStepMaxT = 4;
+constexpr int kStepWarps = 8;
+
+template <int DT, int SDT, int NPT>
+__global__ void __launch_bounds__(32 * kStepWarps)
+ssm_step_kernel(ScanArgs a) {
+    using E = Elem<DT>;
+    using T = typename E::T;
+    const int lane = threadIdx.x & 31;
+    const int64_t c = (int64_t)blockIdx.x * kStepWarps + (threadIdx.x >> 5), b = blockIdx.y;
+    const int64_t d = a.d, N = a.N, Tl = a.T;
+    if (c >= d) return;                                   // whole warps leave together
+    const int64_t ld_bc = a.ld_bc > 0 ? a.ld_bc : N;
+    const T* logA = static_cast<const T*>(a.log_A) + c * N;
+    const float la0 = E::load(logA);
+    const float Abase = -E::rnd(expf(la0));
+    float A2[NPT], ci[NPT], limf[NPT], h[NPT];
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int64_t n = lane + 32 * j;
+        const bool on = n < N;
+        const float la = on ? E::load(logA + n) : 0.f;
+        const float A = on ? -E::rnd(expf(la)) : 0.f;
+        h[j] = 0.f;
+        if (on && a.state_in) {
+            const int64_t si = (b * d + c) * N + n;
+            h[j] = SDT == NT_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.state_in)[si])
+                                  : static_cast<const float*>(a.state_in)[si];
+        }
+        if (on) {
+            if (DT == NT_BF16) {
+                int e2;
+                frexpf(la, &e2);
+                const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
+                if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) ok = false;
+            } else if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) {
+                ok = false;
+            }
+        }
+        const bool lim = on && fabsf(A) < 1e-6f;
+        if (lim) ok = false;
+        limf[j] = lim ? 1.f : 0.f;
+        A2[j] = A * kLog2e;
+        ci[j] = (lim || A == 0.f) ? 0.f : 1.0f / A;
+    }
+    const bool hippo = __all_sync(0xffffffffu, ok);
+    const float rA0 = 1.0f / Abase;
+    const float Dv = E::load(static_cast<const T*>(a.D) + c);
+    const bool sparse_rows = a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
+    const T* p_u = static_cast<const T*>(a.u);
+    const T* p_dt = static_cast<const T*>(a.dt);
+    const T* p_B = static_cast<const T*>(a.Bm);
+    const T* p_C = static_cast<const T*>(a.Cm);
+    const T* p_g = static_cast<const T*>(a.gate);
+    for (int64_t t = 0; t < Tl; ++t) {
+        const int64_t row = b * Tl + t;
+        const float u = E::to_f(p_u[row * d + c]);
+        const float dtv = E::to_f(p_dt[row * d + c]);
+        float y = 0.f;
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int64_t n = lane + 32 * j;
+            if (n >= N) continue;
+            const float Bn = E::to_f(p_B[row * ld_bc + n]);
+            const float Cn = E::to_f(p_C[row * ld_bc + n]);
+            if (hippo) {
+                const float e = ex2(dtv * ((float)(n + 1) * Abase * kLog2e)) - 1.0f;
+                const float tv = __fmaf_rn(Bn * (1.0f / (float)(n + 1)), u * rA0, h[j]);
+                h[j] = __fmaf_rn(e, tv, h[j]);
+            } else {
+                const float av = ex2(dtv * A2[j]);
+                const float coef = __fmaf_rn(dtv, limf[j], __fmaf_rn(av, ci[j], -ci[j]));
+                h[j] = __fmaf_rn(av, h[j], coef * (Bn * u));
+            }
+            y = __fmaf_rn(Cn, h[j], y);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+        if (lane == 0) {
+            const float yv = __fadd_rn(y, __fmul_rn(Dv, u));
+            float o = E::rnd(yv);
+            if (p_g) {
+                const float gv = E::to_f(p_g[row * d + c]);
+                o = E::rnd(o * (a.gate_is_silu ? gv : E::rnd(silu_f(gv))));
+            }
+            int64_t orow = row;
+            if (sparse_rows) orow = a.row_pos[row];
+            if (orow >= 0) static_cast<T*>(a.y)[orow * d + c] = E::from_f(o);
+        }
+    }
+    if (a.state_out) {
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int64_t n = lane + 32 * j;
+            if (n >= N) continue;
+            const int64_t si = (b * d + c) * N + n;
+            if (SDT == NT_BF16) static_cast<__nv_bfloat16*>(a.state_out)[si] = __float2bfloat16_rn(h[j]);
+            else static_cast<float*>(a.state_out)[si] = h[j];
+        }
+    }
+}
+
+template <int DT, int SDT>
+int launch_step(const ScanArgs& a, cudaStream_t stream) {
+    dim3 grid((unsigned)((a.d + kStepWarps - 1) / kStepWarps), (unsigned)a.B);
+    const int npt = a.N <= 32 ? 1 : a.N <= 64 ? 2 : a.N <= 128 ? 4 : 8;
+    switch (npt) {
+        case 1: ssm_step_kernel<DT, SDT, 1><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
+        case 2: ssm_step_kernel<DT, SDT, 2><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
+        case 4: ssm_step_kernel<DT, SDT, 4><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
+        default: ssm_step_kernel<DT, SDT, 8><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
+    }
+    return check_launch("ssm_step_kernel");
+}
+
 }  // namespace
 
 template <int DT>
@@ -624,6 +752,11 @@ int launch_selective_scan_segmented(int dtype, int state_dtype, const ScanArgs& 
 }
 
 int launch_selective_scan(int dtype, int state_dtype, const ScanArgs& a, cudaStream_t stream) {
+    if (a.T <= kStepMaxT && a.N <= 256 && a.B <= 65535) {
+        if (dtype == NT_F32 && state_dtype == NT_F32) return launch_step<NT_F32, NT_F32>(a, stream);
+        if (dtype == NT_BF16 && state_dtype == NT_F32) return launch_step<NT_BF16, NT_F32>(a, stream);
+        if (dtype == NT_BF16 && state_dtype == NT_BF16) return launch_step<NT_BF16, NT_BF16>(a, stream);
+    }
     FusedArgs f{};
     if (dtype == NT_F32 && state_dtype == NT_F32) return launch_mode<NT_F32, NT_F32, 0>(a, f, stream);
     if (dtype == NT_BF16 && state_dtype == NT_F32) return launch_mode<NT_BF16, NT_F32, 0>(a, f, stream);

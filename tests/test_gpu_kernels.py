@@ -151,6 +151,47 @@ def test_selective_scan_general_input_and_T1(nat):
     np.testing.assert_allclose(N(s1), rs1, rtol=1e-4, atol=1e-7)
 
 
+@pytest.mark.parametrize("Nst", [8, 32, 128, 256])
+@pytest.mark.parametrize("hippo", [True, False])
+def test_selective_scan_short_sequences_vs_oracle(nat, Nst, hippo):
+    """T <= 4 (decode steps) runs the one-warp-per-channel step kernel: outputs
+    and carried state against the oracle, with a non-zero carry-in."""
+    rng = np.random.default_rng(Nst + 31 * hippo)
+    for Tn in (1, 2, 4):
+        u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, 3, Tn, 72, Nst, hippo=hippo, limit=not hippo)
+        y, so = nat.selective_scan(T(u), T(dt), T(Bm), T(Cm), T(log_A), T(D), T(st))
+        ry, rs = O.ssm_scan(u, dt, Bm, Cm, log_A, D, st, "fp32")
+        np.testing.assert_allclose(N(y), ry, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(N(so), rs, rtol=1e-4, atol=1e-6)
+
+
+def test_selective_scan_steps_chain_like_one_call(nat):
+    """16 calls of 4 steps with carried state (step kernel) == one 64-step call
+    (chunked kernel), fp32 and bf16 gated with bf16 state."""
+    rng = np.random.default_rng(12)
+    u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, 2, 64, 96, 128)
+    args = [T(a) for a in (u, dt, Bm, Cm)]
+    y, s = nat.selective_scan(*args, T(log_A), T(D), T(st))
+    s_k, ys = T(st), []
+    for k in range(0, 64, 4):
+        yk, s_k = nat.selective_scan(*(a[:, k:k + 4] for a in args), T(log_A), T(D), s_k)
+        ys.append(yk)
+    np.testing.assert_allclose(N(torch.cat(ys, 1)), N(y), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(N(s_k), N(s), rtol=1e-4, atol=1e-6)
+    bf = torch.bfloat16
+    g = T(rng.normal(0, 1, u.shape).astype(np.float32), bf)
+    ab = [a.to(bf) for a in args]
+    yb, sb = nat.selective_scan(*ab, T(log_A, bf), T(D, bf), T(st, bf), gate=g, state_dtype=bf)
+    s_k, ys = T(st, bf), []
+    for k in range(0, 64, 4):
+        yk, s_k = nat.selective_scan(*(a[:, k:k + 4] for a in ab), T(log_A, bf), T(D, bf), s_k,
+                                     gate=g[:, k:k + 4], state_dtype=bf)
+        ys.append(yk)
+    # bf16 state is rounded after every call, so the chained run drifts by bf16 ulps
+    np.testing.assert_allclose(N(torch.cat(ys, 1)), N(yb), rtol=3e-2, atol=3e-2)
+    np.testing.assert_allclose(N(s_k), N(sb), rtol=3e-2, atol=1e-2)
+
+
 def test_selective_scan_streaming_split(nat):
     """Full sequence == two halves with carried state (the reference's continuity test)."""
     rng = np.random.default_rng(6)

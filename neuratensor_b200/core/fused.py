@@ -49,6 +49,10 @@ def rate_like_reference(count: int, numel: int, dtype: torch.dtype) -> float:
 class FusedSpikeBlock(nn.Module):
     """RMSNorm -> in_proj -> LIF -> selective SSM -> gate -> sparse out_proj -> residual."""
 
+    # class of the returned streaming state (the drop-in patch points it at
+    # the reference package's own BlockState)
+    _state_cls = BlockState
+
     def __init__(self, d_model: int, d_state: int = 16, expand: int = 2, beta_init: float = 0.9,
                  learn_beta: bool = True, dropout: float = 0.0) -> None:
         super().__init__()
@@ -97,7 +101,7 @@ class FusedSpikeBlock(nn.Module):
             x, w["norm_w"], w["W_in"], w["beta"], w["threshold"], w["log_A"], w["D"], w["W_proj"], w["b_dt"],
             w["W_out"], w["out_scale"], mem, st, spike_count, sparse=sparse, state_dtype=x.dtype,
             workspace=workspace)
-        return out, BlockState(membrane=mem_out, ssm_state=st_out)
+        return out, self._state_cls(membrane=mem_out, ssm_state=st_out)
 
     def forward(self, x: Tensor, state: Optional[BlockState] = None) -> Tuple[Tensor, BlockState, dict]:
         """x [B, T, d_model] -> (out, BlockState, {"spike_rate", "mean_beta"}) (fused.py:101-147)."""

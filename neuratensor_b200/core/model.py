@@ -116,11 +116,12 @@ class SlidingWindowAttention(nn.Module):
         self._mask = None
 
     def _window_mask(self, T: int, device) -> Tensor:
-        if self._mask is None or self._mask.shape[-1] != T or self._mask.device != device:
+        m = getattr(self, "_mask", None)
+        if m is None or m.shape[-1] != T or m.device != device:
             i = torch.arange(T, device=device)
             rel = i[:, None] - i[None, :]
-            self._mask = ((rel >= 0) & (rel <= self.window))[None, None]
-        return self._mask
+            m = self._mask = ((rel >= 0) & (rel <= self.window))[None, None]
+        return m
 
     def forward(self, x: Tensor) -> Tensor:
         if x.is_cuda and x.dtype == torch.bfloat16 and self.head_dim in (64, 128):
@@ -237,8 +238,9 @@ class NeuraTensorModel(nn.Module):
                    for s in states]
             parts.append(self._forward_rows(input_ids[a:a + g], sub, workspace, last_only))
         logits = torch.cat([p[0] for p in parts])
-        new_states = [BlockState(membrane=torch.cat([p[1][i].membrane for p in parts]),
-                                 ssm_state=torch.cat([p[1][i].ssm_state for p in parts]))
+        state_cls = self.blocks[0]._state_cls
+        new_states = [state_cls(membrane=torch.cat([p[1][i].membrane for p in parts]),
+                                ssm_state=torch.cat([p[1][i].ssm_state for p in parts]))
                       for i in range(len(self.blocks))]
         counts = torch.stack([p[2] for p in parts]).sum(0)
         return logits, new_states, counts

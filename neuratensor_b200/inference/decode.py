@@ -102,4 +102,5 @@ class StepGraph:
     def states(self) -> List[BlockState]:
         """Copies of the carried states (the static buffers change on the next replay)."""
         mem, st = self._split(self.flat.clone())
-        return [BlockState(membrane=m, ssm_state=s) for m, s in zip(mem, st)]
+        state_cls = self.model.blocks[0]._state_cls
+        return [state_cls(membrane=m, ssm_state=s) for m, s in zip(mem, st)]

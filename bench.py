@@ -14,11 +14,11 @@ already in HBM, timed with CUDA events per step (max over ranks), L2 flushed
 between timed steps; ``e2e`` = the same through ``InferenceEngine.run`` with
 the ids copied from pinned host memory and the metrics read back each step;
 ``roofline`` = the selective-scan kernel on one layer of this workload;
-``cpu_baseline`` = the CPU oracle port on a bounded sample of the workload.
+``cpu_baseline`` = the same reference CPU path on a bounded sample.
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-oracle port of NeuraTensor's PyTorch path; the reference itself is not
-available on the GPU host) on the host cores, rank 0 only.
+``--impl reference`` times the reference's own PyTorch path on the host
+cores (NeuraTensor 4.0.4 installed at ``baseline/_ref``; the oracle port of
+that path when it is not installed), rank 0 only, one sequence per step.
 """
 from __future__ import annotations
 
@@ -148,63 +148,100 @@ class Clocks:
                 "reasons": sorted({n for r in self.rows for n in r[2]}), "samples": len(self.rows)}
 
 
+def _reference_package():
+    """The reference package installed at baseline/_ref (NeuraTensor 4.0.4), or None."""
+    path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "neuratensor")):
+        return None
+    os.environ.setdefault("NEURATENSOR_TELEMETRY", "0")
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    try:
+        import neuratensor
+        from neuratensor.inference.engine import InferenceEngine  # noqa: F401
+        return neuratensor
+    except Exception:
+        return None
+
+
+# the reference's own CPU path is timed on one sequence of half the workload's length per step
+REF_T_SAMPLE = 1024
+
+
+class _RefCPU:
+    """The reference's PyTorch path on the host cores (InferenceEngine(device="cpu",
+    dtype=bf16).run, as engine.py:145-178 runs it), with its own seeded weights;
+    the oracle port of that path when the reference package is not installed."""
+
+    def __init__(self):
+        import torch
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.ref = _reference_package()
+        torch.manual_seed(SEED)
+        if self.ref is not None:
+            from neuratensor.core.model import NeuraTensorModel as RefModel
+            from neuratensor.config.presets import get_preset as ref_preset
+            from neuratensor.inference.engine import InferenceEngine as RefEngine
+            self.engine = RefEngine(RefModel(ref_preset(PRESET)), device="cpu", dtype=torch.bfloat16)
+            self.vocab = self.engine.model.config.vocab_size
+            self.kind = "reference"
+        else:
+            from neuratensor_b200 import NeuraTensorModel, get_preset
+            from oracle import neuratensor_oracle as O
+            m = NeuraTensorModel(get_preset(PRESET))
+            self.p = {k: O.bf16(v) for k, v in O.params_from_state_dict(m.state_dict()).items()}
+            c = m.config
+            self.cfg = O.OracleConfig(vocab_size=c.vocab_size, d_model=c.d_model, n_layers=c.n_layers,
+                                      d_state=c.d_state, max_seq_len=c.max_seq_len, attn_every=c.attn_every,
+                                      attn_heads=c.attn_heads, attn_window=c.attn_window)
+            self.vocab = c.vocab_size
+            self.kind = "port"
+        import numpy as np
+        self.rng = np.random.default_rng(SEED)
+
+    def forward(self, T_sample):
+        import torch
+        ids = self.rng.integers(0, self.vocab, (1, T_sample))
+        if self.kind == "reference":
+            self.engine.run(torch.from_numpy(ids), reset_state=True)
+        else:
+            from oracle import neuratensor_oracle as O
+            O.model_forward(ids, self.p, self.cfg, None, "bf16")
+
+    def describe(self, T_sample):
+        if self.kind == "reference":
+            return (f"the reference's own PyTorch path (NeuraTensor 4.0.4 from baseline/_ref, "
+                    f"InferenceEngine(device='cpu', dtype=bf16).run), small preset, B=1 x T={T_sample} per step")
+        return f"oracle port of the reference PyTorch path (numpy, bf16 rounding), B=1 x T={T_sample} per step"
+
+
 def cpu_baseline(budget_s: float = 20.0):
-    """CPU oracle port of the reference path on a bounded sample: small preset bf16, B=1, T=128."""
-    import numpy as np
-    import torch
-    from neuratensor_b200 import NeuraTensorModel, get_preset
-    from oracle import neuratensor_oracle as O
-    torch.manual_seed(SEED)
-    m = NeuraTensorModel(get_preset(PRESET))
-    p = O.params_from_state_dict(m.state_dict())
-    for k in p:
-        p[k] = O.bf16(p[k])
-    c = m.config
-    cfg = O.OracleConfig(vocab_size=c.vocab_size, d_model=c.d_model, n_layers=c.n_layers, d_state=c.d_state,
-                         max_seq_len=c.max_seq_len, attn_every=c.attn_every, attn_heads=c.attn_heads,
-                         attn_window=c.attn_window)
-    rng = np.random.default_rng(SEED)
-    T_sample = 128
+    """The reference's CPU path on a bounded sample of the workload (one sequence)."""
+    r = _RefCPU()
+    T_sample = REF_T_SAMPLE if r.kind == "reference" else 128
     toks, t0 = 0, time.perf_counter()
     while True:
-        ids = rng.integers(0, c.vocab_size, (1, T_sample))
-        O.model_forward(ids, p, cfg, None, "bf16")
+        r.forward(T_sample)
         toks += T_sample
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    return {"value": toks / dt, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
-            "sample": f"oracle (numpy, bf16-rounding emulation) small preset, B=1 x T={T_sample}, "
-                      f"{toks // T_sample} forwards in {dt:.1f} s"}
+    return {"value": toks / dt, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": r.kind,
+            "sample": f"{r.describe(T_sample)}; {toks // T_sample} forwards in {dt:.1f} s"}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
-    import torch
-    torch.set_num_threads(os.cpu_count() or 1)
-    from neuratensor_b200 import NeuraTensorModel, get_preset
-    from oracle import neuratensor_oracle as O
-    torch.manual_seed(SEED)
-    m = NeuraTensorModel(get_preset(PRESET))
-    p = O.params_from_state_dict(m.state_dict())
-    for k in p:
-        p[k] = O.bf16(p[k])
-    c = m.config
-    cfg = O.OracleConfig(vocab_size=c.vocab_size, d_model=c.d_model, n_layers=c.n_layers, d_state=c.d_state,
-                         max_seq_len=c.max_seq_len, attn_every=c.attn_every, attn_heads=c.attn_heads,
-                         attn_window=c.attn_window)
-    rng = np.random.default_rng(SEED)
-    T_sample = 64
+    r = _RefCPU()
+    T_sample = REF_T_SAMPLE if r.kind == "reference" else 64
     for _ in range(args.warmup):
-        O.model_forward(rng.integers(0, c.vocab_size, (1, T_sample)), p, cfg, None, "bf16")
+        r.forward(T_sample)
     times = []
     for _ in range(args.steps):
-        ids = rng.integers(0, c.vocab_size, (1, T_sample))
         t0 = time.perf_counter()
-        O.model_forward(ids, p, cfg, None, "bf16")
+        r.forward(T_sample)
         times.append(time.perf_counter() - t0)
     tot = sum(times)
     v = T_sample * args.steps / tot
@@ -213,10 +250,10 @@ def run_reference(args):
             "warmup": args.warmup, "ms_per_step": 1000 * tot / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "small preset bf16 prefill (sampled: B=1 x T=64 per step on host cores)",
+            "config": {"workload": f"small preset bf16 prefill (sampled on host cores: B=1 x T={T_sample} per step)",
                        "preset": PRESET, "seq_len_sample": T_sample},
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": f"oracle port of the reference PyTorch path, B=1 x T={T_sample} per step"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": r.kind,
+                             "sample": r.describe(T_sample)},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -330,10 +367,10 @@ def run_ours(args):
         clocks = clk.summary()
 
         # spike metrics: NCCL gather of per-rank per-layer counts (off the timed path)
-        tot = ranks.sum_counts(counts)
-        ms = ranks.max_over_ranks(ms, dev)
         di = model.config.d_model * model.config.expand
-        metrics = model.metrics_from_counts(tot.tolist(), GLOBAL_BATCH * SEQ * di, torch.bfloat16)
+        tot, numel = ranks.global_counts(counts, (stop - start) * SEQ * di)
+        ms = ranks.max_over_ranks(ms, dev)
+        metrics = model.metrics_from_counts(tot.tolist(), numel, torch.bfloat16)
 
         # end to end through the public API: pinned host ids -> run() -> metrics on the host
         e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -374,7 +411,9 @@ def run_ours(args):
                    "parallelism": f"dp{world} (batch shards)",
                    "l2": "flushed (256 MiB write) before every timed step"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": GLOBAL_BATCH * SEQ * 8,
-                "d2h_bytes_per_step": 8 * model.config.n_layers * world},
+                "d2h_bytes_per_step": 8 * model.config.n_layers * world,
+                "metrics": "global over all ranks (InferenceEngine.run gathers the spike counts each step)"
+                if world > 1 else "single process"},
         "gpu_launches": launches,
         "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
         "spike_rate": metrics["spike_rate"],

@@ -6,8 +6,15 @@
  * and element strides, runs asynchronously on the given CUDA stream and
  * returns an nt_status code; it never aborts the process.  The caller owns
  * every buffer: inputs, outputs, state buffers and workspaces (sized with
- * the *_workspace_bytes queries).  The library keeps no per-call state, so
- * calls on different streams may run concurrently.
+ * the *_workspace_bytes queries).
+ *
+ * Concurrency: calls on different streams may run concurrently when they use
+ * different workspaces and outputs, with two exceptions that are shared
+ * per device: nt_rmsnorm_in_proj_noalloc's static scratch (overlapping calls
+ * of that entry point race), and the device error word that every kernel
+ * with a bounded wait may set (nt_get_error_flag reports the union of all
+ * streams' flags since it was last cleared).  The launch counter is a process
+ * total.
  *
  * Reference interfaces replaced (paths inside the NeuraTensor source tree):
  *   nt_lif_scan            LIFLayer.forward            neuratensor/core/snn.py:264-312
@@ -145,8 +152,10 @@ NT_API int nt_rmsnorm_in_proj(int dtype, int64_t M, int64_t dm, int64_t di,
  * reserve HBM at start-up and forbid cudaMalloc afterwards.  Requires
  * M*d_model*sizeof(dtype) <= nt_noalloc_scratch_bytes() (else NT_ERR_ARG).
  * The first call on a device, made with that device current, looks up the
- * array's address; make it before any stream capture.  Calls share the array:
- * calls that overlap on the GPU race. */
+ * array's address; make it before any stream capture.  The address is cached
+ * for the life of the process and does not survive a device reset
+ * (cudaDeviceReset or a re-created primary context): do not call this entry
+ * point after one.  Calls share the array: calls that overlap on the GPU race. */
 NT_API size_t nt_noalloc_scratch_bytes(void);
 NT_API int nt_rmsnorm_in_proj_noalloc(int dtype, int64_t M, int64_t dm, int64_t di,
                        const void* x, const void* gamma, const void* W_in,

@@ -21,18 +21,16 @@ class BackendInfo:
     notes: list = field(default_factory=list)
 
     def print(self) -> None:
-        print("=" * 52)
-        print(f"  Backend: {self.name}")
-        print(f"  Device:  {self.device}  dtype={self.dtype}")
+        """One line per known fact about the device and the native library."""
+        rows = [("backend", self.name), ("device", f"{self.device} ({self.dtype})")]
         if self.gpu_name:
-            print(f"  GPU:     {self.gpu_name}")
-            print(f"  CC:      {self.compute_capability}")
-            print(f"  VRAM:    {self.memory_gb:.1f} GB")
-            print(f"  BF16:    {self.bf16}")
-        print(f"  Native:  {self.native_kernels}")
+            rows += [("gpu", f"{self.gpu_name}, compute capability {self.compute_capability}"),
+                     ("memory", f"{self.memory_gb:.1f} GiB"), ("bfloat16", "yes" if self.bf16 else "no")]
+        rows.append(("B200 kernels", "loaded" if self.native_kernels else "not available"))
+        width = max(len(k) for k, _ in rows)
+        print("\n".join(f"{k.rjust(width)} : {v}" for k, v in rows))
         for n in self.notes:
-            print(f"  !  {n}")
-        print("=" * 52)
+            print(f"{'note'.rjust(width)} : {n}")
 
 
 def detect_backend() -> BackendInfo:

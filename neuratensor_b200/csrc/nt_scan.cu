@@ -3,20 +3,18 @@
 // standalone LIF -> selective-scan fusion.
 //
 // Work split: a channel's d_state recurrences are spread over TPC threads
-// (NPT = 8 states each, or 4 when the batch is too small to fill the GPU;
-// TPC = next power of two >= N/NPT).  A 128-thread CTA owns CPB = 128/TPC
-// channels of one batch row and walks time serially.
+// (NPT = 8 states each, or 4 when the batch is too small to give every SM
+// sub-partition a few warps; TPC = next power of two >= N/NPT).  A
+// 128-thread CTA owns CPB = 128/TPC channels of one batch row and walks time
+// serially; the state is float32 in registers for the whole sequence.
 //
-// Per chunk of TCH steps:
-//   1. cp.async stages the next chunk's raw inputs (u or x, dt, gate, B, C)
-//      into shared memory while the current chunk computes (double buffer);
-//   2. the chunk is widened once to float32 work buffers;
-//   3. each thread advances its states through TCH steps from registers
-//      (packed f32x2 arithmetic, branch-free) and writes one partial C.h sum
-//      per step and channel to shared memory -- no shuffles on the serial path;
-//   4. partial sums are reduced per (step, channel), D*u and the gate are
-//      applied, and the chunk is stored with coalesced writes.
-// The state is float32 in registers for the whole sequence.
+// The recurrence is bound by the FP32 pipe (about four fused multiply-adds
+// per state update: the decay chain, the input term, the state update and
+// the C.h readout), so everything else is kept off the per-step path:
+// B/(n+1) and C are widened once per CTA and chunk into a bank-conflict-free
+// layout and read as broadcasts, (u, dt) once per (step, channel), and the
+// partial C.h sums of a channel's TPC threads are combined in registers by a
+// butterfly over TPC steps at a time (no shared-memory reduction).
 //
 // Discretisation per step (A = -exp(log_A)):
 //   A_bar = exp(dt*A)            -> ex2(dt * A*log2(e)) on the MUFU pipe
@@ -94,51 +92,33 @@ __device__ __forceinline__ void static_for(F&& f) {
     }
 }
 
-template <int TPC, int NPT, typename T, int MODE>
-struct ScanSmem {
-    // time steps per staged chunk: 32, or 16 where the channel or state tile is
-    // widest and for the fused op (whose per-step spikes also live in registers)
-    static constexpr int TCH = (TPC == 1 || TPC == 32 || MODE == 1) ? 16 : 32;
-    static constexpr int CPB = 128 / TPC;               // channels per CTA
-    static constexpr int NP = NPT * TPC;                // padded d_state
-    static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;       // elements of T per staging buffer
+// Shared-memory plan of one CTA: CPB channels of one batch row, 128 threads,
+// TPC threads per channel holding NPT states each (NP = TPC*NPT >= d_state).
+template <int TPC, int NPT, typename T>
+struct ScanLayout {
+    static constexpr int TCH = 32;                 // time steps per staged chunk
+    static constexpr int CPB = 128 / TPC;          // channels per CTA
+    static constexpr int NP = TPC * NPT;           // padded d_state
+    // raw staging (double-buffered): u|x, dt, gate tiles [TCH][CPB]; B, C tiles [TCH][NP]
+    static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;
     static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
-    static constexpr int WORK_FLOATS =
-        2 * TCH * CPB + 2 * TCH * NP + TCH * 128 + (MODE == 1 ? TCH * CPB : 0) + CPB + NP + TCH;
-    static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + sizeof(float) * (size_t)WORK_FLOATS;
+    // widened: (u, dt) [TCH][CPB] float2; B/(n+1) and C [TCH][NP] float each;
+    // output tile [TCH][CPB] of T; row positions [TCH]; 1/(n+1) [NP]
+    static constexpr int UD_BYTES = 8 * TCH * CPB;
+    static constexpr int BC_BYTES = 4 * 2 * TCH * NP;
+    static constexpr int YO_BYTES = ((TCH * CPB * (int)sizeof(T)) + 15) & ~15;
+    static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + UD_BYTES + BC_BYTES + YO_BYTES + 4 * TCH + 4 * NP;
 };
 
-// Partial C.h sums: one row of 128 floats per step, channel c's TPC partials
-// contiguous at c*TPC so the reduction reads them as TPC/4 float4s.  Within a
-// channel the float4 groups are XOR-swizzled by yp_x(i), i = step*CPB + c, so
-// the eight threads of a quarter-warp reading group h land in eight distinct
-// bank groups; a warp's per-step stores stay a permutation of 32 consecutive
-// floats.  (The sum does not depend on the order of a channel's groups.)
-template <int TPC>
-__device__ __forceinline__ int yp_x(int i) {
-    constexpr int G = TPC / 4;                       // float4 groups per channel
-    if constexpr (G < 2) return 0;
-    else {
-        constexpr int lg = G == 2 ? 1 : G == 4 ? 2 : 3;
-        return (i >> (3 - lg)) & (G - 1);
-    }
-}
-// Slot of the partial of (step tt, channel cl, sub) in its step's row.
-template <int TPC>
-__device__ __forceinline__ int yp_slot(int tt, int cl, int sub) {
-    constexpr int CPB = 128 / TPC;
-    if constexpr (TPC < 4) return cl * TPC + sub;
-    else return cl * TPC + 4 * ((sub >> 2) ^ yp_x<TPC>(tt * CPB + cl)) + (sub & 3);
-}
-
-// Position of state n within a staged B or C row.  Rows of 64 or more states
-// swap float4 pairs in every other group of eight float4s, so that the eight
-// threads of a quarter-warp reading two float4s each (8 states per thread)
-// hit distinct banks; groups of four states stay contiguous.
-template <int NP>
-__device__ __forceinline__ int bc_swz(int n) {
-    if constexpr (NP >= 64) return n ^ (((n >> 5) & 1) << 2);
-    else return n;
+// Position of logical state n of a staged B or C row: the slices of the TPC
+// threads are interleaved by groups of four states (group q of every thread's
+// slice, then group q+1), so the 16-byte reads of one step by the threads of
+// a warp fall on consecutive bank groups (one wavefront for up to 8 slices;
+// threads of one slice read the same address, a broadcast).
+template <int TPC, int NPT>
+__device__ __forceinline__ int bc_pos(int n) {
+    const int sub = n / NPT, q = (n % NPT) >> 2;
+    return q * 4 * TPC + sub * 4 + (n & 3);
 }
 
 // Widen EPV = 16/sizeof(T) elements (one 16-byte vector) to float32.
@@ -156,38 +136,59 @@ __device__ __forceinline__ void widen16(const __nv_bfloat16* src, float* v) {
     }
 }
 
-// MODE 0: selective scan with given u.  MODE 1: u = LIF spikes of x (fused op).
-// Thread (cl, sub) owns states [NPT*sub, NPT*sub + NPT) of channel c0 + cl.
-#ifndef NT_SCAN_MINB8
-#define NT_SCAN_MINB8 4
-#endif
-#ifndef NT_SCAN_MINB4
-#define NT_SCAN_MINB4 5
-#endif
-// Resident CTAs per SM the register allocation must allow (the recurrence is
-// latency-bound, so warps per SM matter more than hoisting further ahead).
-template <int NPT> struct ScanMinBlocks { static constexpr int value = NPT == 8 ? NT_SCAN_MINB8 : NT_SCAN_MINB4; };
+// Sum of TPC per-step partials across the TPC consecutive lanes of a channel:
+// on entry v[j] is this lane's partial C.h of step j of the group; on exit
+// v[0] is the complete sum for step `sub` (a butterfly reduce-scatter: at
+// each level a lane keeps the half of the steps its bit of `sub` selects and
+// adds the partner's partials for them).
+template <int TPC>
+__device__ __forceinline__ void reduce_scatter(float (&v)[TPC], int sub, unsigned gmask) {
+    static_for<0, 5>([&](auto lv) {
+        constexpr int half = TPC >> (decltype(lv)::value + 1);
+        if constexpr (half >= 1) {
+            const bool upper = (sub & half) != 0;
+#pragma unroll
+            for (int i = 0; i < half; ++i) {
+                const float send = upper ? v[i] : v[i + half];
+                const float keep = upper ? v[i + half] : v[i];
+                v[i] = keep + __shfl_xor_sync(gmask, send, half);
+            }
+        }
+    });
+}
 
-// OUT = 0 (MODE 0 only): the state-only pass of the time-segmented scan --
-// no C, no outputs; writes the segment's end state (float32, from a zero
-// start) to state_out and its total decay exp(A*sum(dt)) per state to
-// a.seg_decay, with the same A the recurrence used.
+// MODE 0: selective scan with given u.  MODE 1: u = LIF spikes of x (fused op).
+// OUT = 0 (MODE 0 only): the state-only pass of the time-segmented scan -- no
+// C, no outputs; writes the segment's end state (float32, from a zero start)
+// to state_out and its total decay exp(A*sum(dt)) per state to a.seg_decay.
+//
+// Thread (cl, sub) owns states [NPT*sub, NPT*sub + NPT) of channel c0 + cl.
+// Per chunk of TCH steps:
+//   1. cp.async stages the next chunk's raw inputs while this one computes;
+//   2. one widening pass per CTA: (u, dt) per (step, channel) -- in MODE 1 one
+//      thread per channel runs the LIF membrane through the chunk here --
+//      and B/(n+1), C per (step, state), shared by every channel of the CTA;
+//   3. each thread advances its states through the chunk from registers, in
+//      groups of TPC steps whose partial C.h sums are combined by a register
+//      butterfly (reduce_scatter); the lane that ends up with step j's sum
+//      adds D*u, applies the gate and writes the output tile;
+//   4. the output tile goes to global memory with 16-byte stores.
 template <int DT, int SDT, int TPC, int NPT, int MODE, int OUT = 1>
-__global__ void __launch_bounds__(128, ScanMinBlocks<NPT>::value)
+__global__ void __launch_bounds__(128, NPT == 8 ? 4 : 5)
 ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     static_assert(OUT == 1 || MODE == 0, "state-only pass is a MODE 0 variant");
+    static_assert(NPT == 4 || NPT == 8, "4 or 8 states per thread");
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    using L = ScanSmem<TPC, NPT, T, MODE>;
-    constexpr int CPB = L::CPB, NP = L::NP, kTch = L::TCH, NPR = NPT / 2;
+    using L = ScanLayout<TPC, NPT, T>;
+    constexpr int CPB = L::CPB, NP = L::NP, kTch = L::TCH, NPR = NPT / 2, NQ = NPT / 4;
+    constexpr int EPV = 16 / (int)sizeof(T);
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float2* w_ud = reinterpret_cast<float2*>(smem_raw + 2 * L::RAW_BYTES);  // [kTch][CPB] (u or x, dt)
-    float* w_B = reinterpret_cast<float*>(w_ud + kTch * CPB);            // [kTch][NP]  B (or B/(n+1))
-    float* w_C = w_B + kTch * NP;                                        // [kTch][NP]
-    float* w_yp = w_C + kTch * NP;                                       // [kTch][128] partial C.h (yp_slot)
-    float* w_s = w_yp + kTch * 128;                                      // [kTch][CPB] spikes (MODE 1 only)
-    float* w_D = w_s + (MODE == 1 ? kTch * CPB : 0);                     // [CPB] skip weights D
-    float* w_rn = w_D + CPB;                                             // [NP] 1/(n+1)
-    int* w_pos = reinterpret_cast<int*>(w_rn + NP);                      // [kTch] compacted row positions
+    float2* w_ud = reinterpret_cast<float2*>(smem_raw + 2 * L::RAW_BYTES);            // [kTch][CPB] (u, dt)
+    float* w_B = reinterpret_cast<float*>(smem_raw + 2 * L::RAW_BYTES + L::UD_BYTES); // [kTch][NP] B/(n+1)
+    float* w_C = w_B + kTch * NP;                                                    // [kTch][NP] C
+    T* w_yo = reinterpret_cast<T*>(smem_raw + 2 * L::RAW_BYTES + L::UD_BYTES + L::BC_BYTES);  // [kTch][CPB]
+    int* w_pos = reinterpret_cast<int*>(smem_raw + 2 * L::RAW_BYTES + L::UD_BYTES + L::BC_BYTES + L::YO_BYTES);
+    float* w_rn = reinterpret_cast<float*>(w_pos + kTch);                            // [NP] 1/(n+1)
 
     const int64_t T_len = MODE ? f.L : a.T, d = MODE ? f.d : a.d, N = MODE ? f.N : a.N;
     const T* p_u = static_cast<const T*>(MODE ? f.x : a.u);
@@ -198,7 +199,8 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     const bool has_gate = p_g != nullptr;
     const int64_t ld_bc = (MODE == 0 && a.ld_bc > 0) ? a.ld_bc : N;
 
-    const int tid = threadIdx.x, cl = tid / TPC, sub = tid % TPC;
+    const int tid = threadIdx.x, cl = tid / TPC, sub = tid % TPC, lane = tid & 31;
+    const unsigned gmask = TPC >= 32 ? 0xffffffffu : (((1u << TPC) - 1u) << (lane & ~(TPC - 1)));
     const int64_t c0 = (int64_t)blockIdx.x * CPB, c = c0 + cl, b = blockIdx.y;
     const bool live = c < d;
 
@@ -209,13 +211,12 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         return f.log_A[c * N + n];
     };
     auto A_of = [&](float la) -> float { return MODE == 0 ? -Elem<DT>::rnd(expf(la)) : -expf(la); };
-    // HiPPO structure test.  fp32 parameters: A[c,n] == (n+1)*A[c,0] to 1e-6
-    // relative.  bf16 parameters: log_A[c,n] == log(n+1) + log_A[c,0] to one
-    // bf16 ulp of the stored value, i.e. the parameter is the HiPPO init up to
-    // its own storage rounding.
+    // HiPPO structure test, per channel.  fp32 parameters: A[c,n] == (n+1)*A[c,0]
+    // to 1e-6 relative.  bf16 parameters: log_A[c,n] == log(n+1) + log_A[c,0] to
+    // one bf16 ulp of the stored value (the HiPPO init up to storage rounding).
     constexpr bool kBf16Params = (MODE == 0 && DT == NT_BF16);
-    float A2[NPT], cinv[NPT], h[NPT];
-    unsigned lim_mask = 0;
+    float A2[NPT], h[NPT];
+    float2 ci2[NPR], lim2[NPR];
     bool hippo_ok = true;
     const float la0 = live ? load_logA(0) : 0.f;
     const float Abase = live ? A_of(la0) : -1.f;
@@ -244,41 +245,39 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             }
         }
         const bool lim = on && fabsf(A) < 1e-6f;
-        if (lim) { lim_mask |= 1u << j; hippo_ok = false; }
+        if (lim) hippo_ok = false;
         A2[j] = A * kLog2e;
-        cinv[j] = (lim || A == 0.f) ? 0.f : 1.0f / A;   // limit states take B_bar = dt*B
+        // general path on B' = B/(n+1): B_bar*u = (A_bar - 1) * ((n+1)/A) * B' * u,
+        // or dt * (n+1) * B' * u for the |A| < 1e-6 states (ssm.py:129-137)
+        const float np1 = (float)(n + 1);
+        const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
+        if (j & 1) { ci2[j / 2].y = ci; lim2[j / 2].y = lim ? np1 : 0.f; }
+        else { ci2[j / 2].x = ci; lim2[j / 2].x = lim ? np1 : 0.f; }
     }
-    const bool hippo = __syncthreads_and(hippo_ok ? 1 : 0) != 0;
+    // one decision per channel: every state of the channel must qualify
+    const unsigned okm = __ballot_sync(0xffffffffu, hippo_ok);
+    const bool hippo = (okm & gmask) == gmask;
     // HiPPO constants: first-state exponent, ratio exponent, 1/A[c,0]
     const float a2first = (float)(sub * NPT + 1) * Abase * kLog2e;
     const float q2 = Abase * kLog2e;
     const float rA0 = 1.0f / Abase;
-    float2 ci2[NPR], nci2[NPR], lim2[NPR];
-#pragma unroll
-    for (int j = 0; j < NPR; ++j) {
-        ci2[j] = make_float2(cinv[2 * j], cinv[2 * j + 1]);
-        nci2[j] = make_float2(-cinv[2 * j], -cinv[2 * j + 1]);
-        lim2[j] = make_float2((lim_mask >> (2 * j)) & 1u ? 1.f : 0.f, (lim_mask >> (2 * j + 1)) & 1u ? 1.f : 0.f);
-    }
-    float beta = 0.f, th = 0.f, mem = 0.f;
-    float dt_sum = 0.f;                          // state-only pass: sum of dt over the segment
-    if (MODE == 1 && live) {
-        beta = f.beta[c];
-        th = f.threshold[c];
-        if (f.mem_in) mem = f.mem_in[b * d + c];
-    }
-    for (int i = tid; i < NP; i += 128) w_rn[i] = 1.0f / (float)(i + 1);
-    for (int i = tid; i < CPB; i += 128) {
-        const int64_t cg = c0 + i;
-        w_D[i] = cg < d ? (MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + cg) : f.Dskip[cg])
-                        : 0.f;
+    float Dv = 0.f;
+    if (live) Dv = MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + c) : f.Dskip[c];
+
+    float beta = 0.f, th = 0.f, mem = 0.f;          // MODE 1: thread tid < CPB runs channel c0 + tid's LIF
+    const int64_t cm = c0 + tid;
+    if (MODE == 1 && tid < CPB && cm < d) {
+        beta = f.beta[cm];
+        th = f.threshold[cm];
+        if (f.mem_in) mem = f.mem_in[b * d + cm];
     }
     unsigned spike_local = 0;
+    float dt_sum = 0.f;                             // state-only pass: sum of dt over the segment
+    for (int i = tid; i < NP; i += 128) w_rn[i] = 1.0f / (float)(i + 1);
     const bool sparse_rows = (MODE == 0) && a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
 
     // 16-byte staging is possible when every tile row starts 16-byte aligned
-    constexpr int EPV = 16 / (int)sizeof(T);
-    const bool act_vec = (d % EPV == 0) && (c0 + CPB <= d) &&
+    const bool act_vec = (d % EPV == 0) && (c0 + CPB <= d) && (CPB % EPV == 0) &&
                          ((reinterpret_cast<uintptr_t>(p_u) | reinterpret_cast<uintptr_t>(p_dt) |
                            reinterpret_cast<uintptr_t>(p_g)) & 15) == 0;
     const bool bc_vec = (NP == N) && (ld_bc % EPV == 0) &&
@@ -300,51 +299,36 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         cp_async_commit();
     };
 
-    // one step; steps past the end of the sequence see u = dt = B = 0, which
-    // leaves the state unchanged (A_bar = 1, no input term)
-    // One step.  The step's partial C.h (and, in MODE 1, its spike) go to
-    // registers; they reach shared memory only after the whole chunk, so no
-    // store sits between one step's loads and the next step's (the compiler can
-    // then overlap the independent exponentials and loads of successive steps).
-    auto step = [&](int tt, int nt, auto hip, float& yp_out, float& u_out) {
+    // One step of this thread's NPT states.  Steps past the end of the
+    // sequence see u = dt = B = 0, which leaves the state unchanged.
+    auto step = [&](int tt, auto hip) -> float {
         constexpr bool HIP = decltype(hip)::value;
         float Bf[NPT], Cf[NPT];
 #pragma unroll
-        for (int q = 0; q < NPT / 4; ++q) {
-            const int n4 = bc_swz<NP>(sub * NPT + 4 * q);
-            const float4 bq = *reinterpret_cast<const float4*>(w_B + tt * NP + n4);
+        for (int q = 0; q < NQ; ++q) {
+            const int o = tt * NP + q * 4 * TPC + sub * 4;
+            const float4 bq = *reinterpret_cast<const float4*>(w_B + o);
             Bf[4 * q] = bq.x; Bf[4 * q + 1] = bq.y; Bf[4 * q + 2] = bq.z; Bf[4 * q + 3] = bq.w;
             if (OUT) {
-                const float4 cq = *reinterpret_cast<const float4*>(w_C + tt * NP + n4);
+                const float4 cq = *reinterpret_cast<const float4*>(w_C + o);
                 Cf[4 * q] = cq.x; Cf[4 * q + 1] = cq.y; Cf[4 * q + 2] = cq.z; Cf[4 * q + 3] = cq.w;
             }
         }
         const float2 ud = w_ud[tt * CPB + cl];
-        float u;
-        if (MODE == 0) {
-            u = ud.x;
-        } else {
-            // LIF step (snn.py:177-181) in fp32, identical in every thread of the channel
-            const float m1 = __fadd_rn(__fmul_rn(beta, mem), ud.x);
-            const float s1 = (m1 >= th) ? 1.f : 0.f;
-            const float m2 = __fsub_rn(m1, __fmul_rn(th, s1));
-            const bool in_seq = tt < nt;
-            u = in_seq ? s1 : 0.f;
-            mem = in_seq ? m2 : mem;
-        }
-        const float dtv = ud.y;
+        const float u = ud.x, dtv = ud.y;
         float2 av[NPR], hv[NPR];
 #pragma unroll
         for (int j = 0; j < NPR; ++j) hv[j] = make_float2(h[2 * j], h[2 * j + 1]);
         if (HIP) {
             // A[n] = (n+1) A0.  With e = A_bar - 1 = exp(dt A[n]) - 1 and
-            // w = u/A0 * B/(n+1) = u * B_bar / e, the update A_bar h + B_bar u is
-            //     h' = h + e (h + w)      (two fmas: t = B/(n+1) * u/A0 + h, h + e t)
+            // w = u B/((n+1) A0) = u B_bar / e, the update A_bar h + B_bar u is
+            //     h' = h + e (h + w)      (two fmas: t = B' * u/A0 + h, h + e t)
             // and e follows the chain e[n+1] = e[n] q + (q - 1), q = exp(dt A0).
             const float e0 = ex2(dtv * a2first) - 1.0f;
             const float qv = ex2(dtv * q2);
             av[0] = make_float2(e0, __fmaf_rn(e0, qv, qv - 1.0f));
-            const float2 qq = make_float2(qv * qv, qv * qv);
+            const float qs = qv * qv;
+            const float2 qq = make_float2(qs, qs);
             const float qm = __fmaf_rn(qv, qv, -1.0f);
             const float2 qqm = make_float2(qm, qm);
 #pragma unroll
@@ -362,8 +346,8 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             const float2 uu = make_float2(u, u), dd = make_float2(dtv, dtv);
 #pragma unroll
             for (int j = 0; j < NPR; ++j) {
-                // (A_bar - 1)/A as one fma; states with |A| < 1e-6 use dt instead
-                const float2 coef = __ffma2_rn(dd, lim2[j], __ffma2_rn(av[j], ci2[j], nci2[j]));
+                const float2 nci = make_float2(-ci2[j].x, -ci2[j].y);
+                const float2 coef = __ffma2_rn(dd, lim2[j], __ffma2_rn(av[j], ci2[j], nci));
                 const float2 bu = __fmul2_rn(coef, __fmul2_rn(make_float2(Bf[2 * j], Bf[2 * j + 1]), uu));
                 hv[j] = __ffma2_rn(av[j], hv[j], bu);
             }
@@ -375,12 +359,11 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             float2 y2 = __fmul2_rn(make_float2(Cf[0], Cf[1]), hv[0]);
 #pragma unroll
             for (int j = 1; j < NPR; ++j) y2 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y2);
-            yp_out = y2.x + y2.y;
+            return y2.x + y2.y;
         } else {
-            yp_out = 0.f;
             dt_sum += dtv;                         // the segment's total decay exponent
+            return 0.f;
         }
-        u_out = u;
     };
 
     const int nchunks = (int)((T_len + kTch - 1) / kTch);
@@ -394,111 +377,123 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
             cp_async_wait<0>();
         }
         __syncthreads();
-        // ---- widen the chunk to float32 (B pre-divided by n+1 on the HiPPO path)
+        const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
+        // ---- widening pass --------------------------------------------------
         const T* rb = raw_buf(kc);
-        for (int i = tid * EPV; i < kTch * CPB; i += 128 * EPV) {
-            float uv[EPV], dv[EPV];
-            widen16(rb + i, uv);
-            widen16(rb + kTch * CPB + i, dv);
+        const T* r_u = rb;
+        const T* r_dt = r_u + kTch * CPB;
+        const T* r_g = r_dt + kTch * CPB;
+        const T* r_B = r_g + kTch * CPB;
+        const T* r_C = r_B + kTch * NP;
+        if (MODE == 0) {
+            for (int i = tid * EPV; i < kTch * CPB; i += 128 * EPV) {
+                float uv[EPV], dv[EPV];
+                widen16(r_u + i, uv);
+                widen16(r_dt + i, dv);
 #pragma unroll
-            for (int k = 0; k < EPV; k += 2)
-                *reinterpret_cast<float4*>(w_ud + i + k) = make_float4(uv[k], dv[k], uv[k + 1], dv[k + 1]);
+                for (int k = 0; k < EPV; k += 2)
+                    *reinterpret_cast<float4*>(w_ud + i + k) = make_float4(uv[k], dv[k], uv[k + 1], dv[k + 1]);
+            }
+        } else if (tid < CPB) {
+            // LIF (snn.py:177-181) in fp32 for channel c0 + tid through the chunk;
+            // steps past the sequence end give u = 0 and leave the membrane alone
+            const bool on = cm < d;
+#pragma unroll 4
+            for (int tt = 0; tt < kTch; ++tt) {
+                const float xv = to_f(r_u[tt * CPB + tid]);
+                const float m1 = __fadd_rn(__fmul_rn(beta, mem), xv);
+                const float s1 = (m1 >= th) ? 1.f : 0.f;
+                const bool in_seq = on && tt < nt;
+                const float uu = in_seq ? s1 : 0.f;
+                mem = in_seq ? __fsub_rn(m1, __fmul_rn(th, s1)) : mem;
+                w_ud[tt * CPB + tid] = make_float2(uu, to_f(r_dt[tt * CPB + tid]));
+                if (in_seq) {
+                    spike_local += uu != 0.f;
+                    if (f.spikes) {
+                        const int64_t idx = (row0 + t0 + tt) * d + cm;
+                        if (f.spike_dtype == NT_U8) static_cast<unsigned char*>(f.spikes)[idx] = (unsigned char)(uu != 0.f);
+                        else static_cast<__nv_bfloat16*>(f.spikes)[idx] = __float2bfloat16_rn(uu);
+                    }
+                }
+            }
         }
         for (int i = tid * EPV; i < kTch * NP; i += 128 * EPV) {
             float bv[EPV], cv[EPV];
-            widen16(rb + 3 * kTch * CPB + i, bv);
-            if (OUT) widen16(rb + 3 * kTch * CPB + kTch * NP + i, cv);
+            widen16(r_B + i, bv);
+            if (OUT) widen16(r_C + i, cv);
 #pragma unroll
             for (int k = 0; k < EPV; k += 4) {
                 const int tt = (i + k) / NP, n = (i + k) % NP;     // four states of one row
-                const int o = tt * NP + bc_swz<NP>(n);
-                float4 b4 = make_float4(bv[k], bv[k + 1], bv[k + 2], bv[k + 3]);
-                if (hippo) {
-                    const float4 r4 = *reinterpret_cast<const float4*>(w_rn + n);
-                    b4.x *= r4.x; b4.y *= r4.y; b4.z *= r4.z; b4.w *= r4.w;
-                }
-                *reinterpret_cast<float4*>(w_B + o) = b4;
+                const int o = tt * NP + bc_pos<TPC, NPT>(n);
+                const float4 r4 = *reinterpret_cast<const float4*>(w_rn + n);
+                *reinterpret_cast<float4*>(w_B + o) =
+                    make_float4(bv[k] * r4.x, bv[k + 1] * r4.y, bv[k + 2] * r4.z, bv[k + 3] * r4.w);
                 if (OUT) *reinterpret_cast<float4*>(w_C + o) = make_float4(cv[k], cv[k + 1], cv[k + 2], cv[k + 3]);
             }
         }
         if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
         __syncthreads();
-        // ---- recurrence: fixed-length, fully unrolled runs of kRun steps --------
-        // (each run's partial sums stay in registers and are stored after it)
-        const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
-        constexpr int kRun = kTch < 16 ? kTch : 16;
-        static_for<0, kTch / kRun>([&](auto run) {
-            constexpr int r0 = decltype(run)::value * kRun;
-            float ypr[kRun], upr[kRun];
-            if (hippo) static_for<0, kRun>([&](auto j) { constexpr int q = decltype(j)::value; step(r0 + q, nt, std::true_type{}, ypr[q], upr[q]); });
-            else static_for<0, kRun>([&](auto j) { constexpr int q = decltype(j)::value; step(r0 + q, nt, std::false_type{}, ypr[q], upr[q]); });
-            if constexpr (OUT) {
-#pragma unroll
-                for (int q = 0; q < kRun; ++q) {
-                    w_yp[(r0 + q) * 128 + yp_slot<TPC>(r0 + q, cl, sub)] = ypr[q];
-                    if (MODE == 1) w_s[(r0 + q) * CPB + cl] = upr[q];   // every thread of the channel stores the same value
+        // ---- recurrence: groups of TPC steps, partial sums combined in registers
+        auto run = [&](auto hip) {
+            static_for<0, kTch / TPC>([&](auto grp) {
+                constexpr int g0 = decltype(grp)::value * TPC;
+                float yp[TPC];
+                static_for<0, TPC>([&](auto j) { yp[decltype(j)::value] = step(g0 + decltype(j)::value, hip); });
+                if constexpr (OUT) {
+                    if constexpr (TPC > 1) reduce_scatter<TPC>(yp, sub, gmask);
+                    const int tt = g0 + (TPC > 1 ? sub : 0);
+                    const float uu = w_ud[tt * CPB + cl].x;
+                    const float yv = __fadd_rn(yp[0], __fmul_rn(Dv, uu));
+                    if (MODE == 0) {
+                        using E = Elem<DT>;
+                        float o = E::rnd(yv);
+                        if (has_gate) {
+                            const float gv = to_f(r_g[tt * CPB + cl]);
+                            o = E::rnd(o * (a.gate_is_silu ? gv : E::rnd(silu_f(gv))));
+                        }
+                        w_yo[tt * CPB + cl] = E::from_f(o);
+                    } else {
+                        w_yo[tt * CPB + cl] = __float2bfloat16_rn(yv);
+                    }
                 }
-            }
-        });
-        __syncthreads();
+            });
+        };
+        if (hippo) run(std::true_type{});
+        else run(std::false_type{});
         if constexpr (OUT) {
-        // ---- reduce partial sums, D*u, gate; coalesced stores -----------------
-        // thread tid covers channel tid % CPB of steps tid / CPB + k*TPC
-#pragma unroll 1
-        for (int k = 0; k < (kTch * CPB + 127) / 128; ++k) {
-            const int i = tid + 128 * k;
-            if ((kTch * CPB) % 128 != 0 && i >= kTch * CPB) break;
-            const int tt = tid / CPB + k * TPC, cc = tid % CPB;
-            const int64_t t = t0 + tt, cg = c0 + cc;
-            if (tt >= nt || cg >= d) continue;
-            float yp;
-            const float* yrow = w_yp + tt * 128 + cc * TPC;
-            if constexpr (TPC == 1) {
-                yp = yrow[0];
-            } else if constexpr (TPC == 2) {
-                const float2 p = *reinterpret_cast<const float2*>(yrow);
-                yp = p.x + p.y;
+            __syncthreads();
+            // ---- output tile -> global (16-byte stores where rows allow) -------
+            constexpr int VPR = (CPB * (int)sizeof(T)) % 16 == 0 ? CPB * (int)sizeof(T) / 16 : 1;
+            constexpr bool kRowVec = (CPB * (int)sizeof(T)) % 16 == 0;
+            using OT = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
+            OT* p_y = static_cast<OT*>(MODE ? f.y : a.y);
+            const bool vec_out = kRowVec && act_vec && (reinterpret_cast<uintptr_t>(p_y) & 15) == 0;
+            if (vec_out) {
+                for (int i = tid; i < kTch * VPR; i += 128) {
+                    const int tt = i / VPR, v = i % VPR;
+                    if (tt >= nt) continue;
+                    int64_t row = row0 + t0 + tt;
+                    if (sparse_rows) {
+                        row = w_pos[tt];
+                        if (row < 0) continue;
+                    }
+                    *reinterpret_cast<uint4*>(p_y + row * d + c0 + v * EPV) =
+                        *reinterpret_cast<const uint4*>(w_yo + tt * CPB + v * EPV);
+                }
             } else {
-                // TPC/4 float4 groups (swizzled order), summed as packed pairs
-                const int x = yp_x<TPC>(i);
-                const float4 p0 = *reinterpret_cast<const float4*>(yrow + 4 * x);
-                float2 s0 = make_float2(p0.x, p0.y), s1 = make_float2(p0.z, p0.w);
-#pragma unroll
-                for (int g = 1; g < TPC / 4; ++g) {
-                    const float4 p = *reinterpret_cast<const float4*>(yrow + 4 * (g ^ x));
-                    s0 = __fadd2_rn(s0, make_float2(p.x, p.y));
-                    s1 = __fadd2_rn(s1, make_float2(p.z, p.w));
+                for (int i = tid; i < kTch * CPB; i += 128) {
+                    const int tt = i / CPB, cc = i % CPB;
+                    if (tt >= nt || c0 + cc >= d) continue;
+                    int64_t row = row0 + t0 + tt;
+                    if (sparse_rows) {
+                        row = w_pos[tt];
+                        if (row < 0) continue;
+                    }
+                    p_y[row * d + c0 + cc] = w_yo[tt * CPB + cc];
                 }
-                s0 = __fadd2_rn(s0, s1);
-                yp = s0.x + s0.y;
-            }
-            const float uu = MODE == 0 ? w_ud[i].x : w_s[i];
-            const float yv = __fadd_rn(yp, __fmul_rn(w_D[cc], uu));
-            int64_t row = row0 + t;
-            if (MODE == 0) {
-                using E = Elem<DT>;
-                float o = E::rnd(yv);
-                if (has_gate) {
-                    const float gv = to_f(rb[2 * kTch * CPB + i]);
-                    o = E::rnd(o * (a.gate_is_silu ? gv : E::rnd(silu_f(gv))));
-                }
-                if (sparse_rows) {
-                    const int pos = w_pos[tt];
-                    if (pos < 0) continue;
-                    row = pos;
-                }
-                static_cast<typename E::T*>(a.y)[row * d + cg] = E::from_f(o);
-            } else {
-                static_cast<__nv_bfloat16*>(f.y)[row * d + cg] = __float2bfloat16_rn(yv);
-                if (f.spikes) {
-                    if (f.spike_dtype == NT_U8) static_cast<unsigned char*>(f.spikes)[row * d + cg] = (unsigned char)(uu != 0.f);
-                    else static_cast<__nv_bfloat16*>(f.spikes)[row * d + cg] = __float2bfloat16_rn(uu);
-                }
-                spike_local += (uu != 0.f);
             }
         }
-        }   // OUT
-        __syncthreads();   // raw_buf(kc) is refilled by the next iteration's issue
+        __syncthreads();   // raw_buf(kc) and the tiles are refilled by the next chunk
     }
     // ---- carry-out -----------------------------------------------------------
     if constexpr (!OUT) {
@@ -528,7 +523,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         }
     }
     if (MODE == 1) {
-        if (live && sub == 0 && f.mem_out) f.mem_out[b * d + c] = mem;
+        if (tid < CPB && cm < d && f.mem_out) f.mem_out[b * d + cm] = mem;
         if (f.spike_count) {
             const unsigned w = __reduce_add_sync(0xffffffffu, spike_local);
             if ((tid & 31) == 0 && w) atomicAdd(f.spike_count, (unsigned long long)w);
@@ -545,7 +540,7 @@ int pow2_at_least(int64_t x) {
 template <int DT, int SDT, int MODE, int TPC, int NPT, int OUT>
 int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    using L = ScanSmem<TPC, NPT, T, MODE>;
+    using L = ScanLayout<TPC, NPT, T>;
     auto kern = ssm_scan_kernel<DT, SDT, TPC, NPT, MODE, OUT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
@@ -555,12 +550,13 @@ int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     return check_launch("ssm_scan_kernel");
 }
 
-#ifndef NT_SCAN_NARROW_CTAS
-#define NT_SCAN_NARROW_CTAS 4
+#ifndef NT_SCAN_NARROW_WARPS
+#define NT_SCAN_NARROW_WARPS 3
 #endif
-// States per thread: 8, or 4 when 8 would leave the GPU with fewer than four
-// 128-thread CTAs per SM (the recurrence is latency-bound, so warps matter
-// more than the extra per-thread work of a narrower state slice).
+// States per thread: 8, or 4 when 8 would give the GPU fewer than
+// NT_SCAN_NARROW_WARPS warps per SM sub-partition: the recurrence of one warp
+// is a serial chain over T, so a sub-partition with one warp more than its
+// neighbours sets the kernel's time, and halving the slice doubles the warps.
 template <int DT, int SDT, int MODE, int OUT = 1>
 int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     const int64_t N = MODE ? f.N : a.N, d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
@@ -568,10 +564,11 @@ int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tpc8 = pow2_at_least((N + 7) / 8);
-    const int64_t ctas8 = B * ((d + 128 / tpc8 - 1) / (128 / tpc8));
-    const bool narrow = N >= 8 && tpc8 <= 16 && ctas8 < (int64_t)NT_SCAN_NARROW_CTAS * sms;
-    if (narrow) {
+    const int64_t warps8 = B * ((d + 128 / tpc8 - 1) / (128 / tpc8)) * 4;
+    const bool narrow = N > 4 && tpc8 <= 16 && warps8 < (int64_t)NT_SCAN_NARROW_WARPS * 4 * sms;
+    if (narrow || N <= 4) {
         switch (pow2_at_least((N + 3) / 4)) {
+            case 1: return launch_tpc<DT, SDT, MODE, 1, 4, OUT>(a, f, stream);
             case 2: return launch_tpc<DT, SDT, MODE, 2, 4, OUT>(a, f, stream);
             case 4: return launch_tpc<DT, SDT, MODE, 4, 4, OUT>(a, f, stream);
             case 8: return launch_tpc<DT, SDT, MODE, 8, 4, OUT>(a, f, stream);

@@ -25,6 +25,7 @@ from torch import Tensor
 from ..config.presets import get_preset
 from ..core.fused import BlockState
 from ..core.model import ModelConfig, NeuraTensorModel
+from . import ranks
 
 
 @dataclass
@@ -53,7 +54,7 @@ class InferenceEngine:
     """Device placement, precision, streaming state and benchmarking around the model."""
 
     def __init__(self, model: NeuraTensorModel, device: Optional[str] = None, dtype: Optional[torch.dtype] = None,
-                 compile_model: bool = False) -> None:
+                 compile_model: bool = False, distributed: Optional[bool] = None) -> None:
         self.device = device or _best_device()
         if not self.device.startswith("cuda"):
             raise RuntimeError("neuratensor_b200 runs on CUDA (sm_100) only; got device=" + self.device)
@@ -62,6 +63,15 @@ class InferenceEngine:
         # run() replays one captured CUDA graph per input shape (see inference/decode.py);
         # False launches the kernels one by one (same kernels, same results)
         self.use_graphs = True
+        # Under torchrun (one process per GPU, each running its own rows of the
+        # batch) run() returns the metrics of the whole global batch, as one
+        # process over all rows would (model.py:286-291): the per-layer spike
+        # counts and element counts are summed over the ranks.  Default: on
+        # when a process group with more than one rank is initialised.
+        if distributed is None:
+            import torch.distributed as dist
+            distributed = dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+        self.distributed = bool(distributed)
         model = model.to(self.device).to(self.dtype)
         model.eval()
         self.model = model
@@ -112,9 +122,14 @@ class InferenceEngine:
         t0 = time.perf_counter()
         with torch.autocast(device_type="cuda", dtype=self.dtype, enabled=self.dtype != torch.float32):
             if self.use_graphs and ids.is_cuda:
-                logits, new_states, metrics = self._run_graph(ids)
+                logits, new_states, counts = self._run_graph(ids)
             else:
-                logits, new_states, metrics = self.model(ids, self._states)
+                logits, new_states, counts = self.model.forward_device(ids, self._states)
+        B, T = logits.shape[:2]
+        numel = B * T * self.model.config.d_model * self.model.config.expand
+        if self.distributed:
+            counts, numel = ranks.global_counts(counts, numel)
+        metrics = self.model.metrics_from_counts(counts.tolist(), numel, logits.dtype)
         torch.cuda.synchronize(self.device)
         latency_ms = (time.perf_counter() - t0) * 1000.0
         self._states = new_states
@@ -128,9 +143,7 @@ class InferenceEngine:
         g = self.model.step_graph(B, T, ids.device, self.dtype)
         g.load_states(self._states)
         logits = g.replay(ids).clone()
-        di = self.model.config.d_model * self.model.config.expand
-        metrics = self.model.metrics_from_counts(g.counts.tolist(), B * T * di, logits.dtype)
-        return logits, g.states(), metrics
+        return logits, g.states(), g.counts.clone()
 
     @torch.no_grad()
     def generate(self, input_ids: Tensor, max_new_tokens: int = 64, temperature: float = 1.0, top_k: int = 50,

@@ -49,6 +49,20 @@ def sum_counts(counts: torch.Tensor) -> torch.Tensor:
     return torch.stack(parts).sum(0)
 
 
+def global_counts(counts: torch.Tensor, numel: int) -> Tuple[torch.Tensor, int]:
+    """Per-layer spike counts and the per-layer element count summed over all
+    ranks, so that count / numel is the reference's spike rate over the whole
+    global batch (ranks may hold different numbers of rows)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return counts, int(numel)
+    v = torch.cat([counts.reshape(-1).to(torch.int64),
+                   torch.tensor([int(numel)], dtype=torch.int64, device=counts.device)])
+    parts = [torch.zeros_like(v) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, v)
+    tot = torch.stack(parts).sum(0)
+    return tot[:-1], int(tot[-1].item())
+
+
 def max_over_ranks(value: float, device: torch.device) -> float:
     """The largest `value` over all ranks (the job's time is its slowest rank's)."""
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:

@@ -26,6 +26,8 @@
  *   nt_rmsnorm_in_proj     FusedSpikeBlock.norm + in_proj    neuratensor/core/fused.py:118-119
  *   nt_block_forward       FusedSpikeBlock.forward     neuratensor/core/fused.py:101-147
  *   nt_window_attention    SlidingWindowAttention RoPE + SDPA neuratensor/core/model.py:148-178
+ *   nt_embedding           NeuraTensorModel.embedding  neuratensor/core/model.py:258
+ *   nt_lm_head             NeuraTensorModel.norm + lm_head neuratensor/core/model.py:283-284
  *   nt_lif_ssm_fused       LIF spikes driving the selective scan with given dt/B/C
  *                          (snn.py:167-182 feeding ssm.py:106-139,184-221)
  *
@@ -160,6 +162,22 @@ NT_API size_t nt_noalloc_scratch_bytes(void);
 NT_API int nt_rmsnorm_in_proj_noalloc(int dtype, int64_t M, int64_t dm, int64_t di,
                        const void* x, const void* gamma, const void* W_in,
                        void* h, void* gate, void* stream);
+
+/* Embedding gather -- NeuraTensorModel.embedding (model.py:258, nn.Embedding):
+ * out[r, :] = W[ids[r], :] for r < M.  ids: [M] int64; W: [vocab, dm]; out:
+ * [M, dm], both `dtype`.  An id outside [0, vocab) yields a zero row and sets
+ * a flag in the device error word (nt_get_error_flag), where the reference
+ * raises IndexError. */
+NT_API int nt_embedding(int dtype, int64_t M, int64_t dm, int64_t vocab, const int64_t* ids, const void* W,
+                        void* out, void* stream);
+
+/* Final RMSNorm + tied lm_head -- NeuraTensorModel.norm + lm_head
+ * (model.py:283-284): logits = RMSNorm(x) W^T, logits in `dtype` (bf16 logits
+ * in bf16 mode).  x: [M, dm]; gamma: [dm]; W: [vocab, dm] (the embedding
+ * matrix when tied); logits: [M, vocab].  Workspace: nt_lm_head_workspace_bytes(). */
+NT_API int64_t nt_lm_head_workspace_bytes(int dtype, int64_t M, int64_t dm, int64_t vocab);
+NT_API int nt_lm_head(int dtype, int64_t M, int64_t dm, int64_t vocab, const void* x, const void* gamma,
+                      const void* W, void* logits, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* FusedSpikeBlock.forward in eval mode (fused.py:101-147):
  *   out = sparse_out_proj(SSM(LIF(in_proj(RMSNorm(x))_h)) * silu(gate)) * out_scale + x

@@ -47,7 +47,12 @@ def _deps_mtime() -> float:
 
 
 def up_to_date() -> bool:
-    return os.path.exists(LIB) and os.path.getmtime(LIB) >= _deps_mtime()
+    """The library is newer than every source, header and object it is made of."""
+    if not os.path.exists(LIB):
+        return False
+    objs = [os.path.join(BUILD, f) for f in os.listdir(BUILD)] if os.path.isdir(BUILD) else []
+    newest = max([_deps_mtime()] + [os.path.getmtime(o) for o in objs if o.endswith(".o")])
+    return os.path.getmtime(LIB) >= newest
 
 
 def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) -> str:
@@ -58,8 +63,16 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
     cc = nvcc()
     extra = ["-Xptxas", "-v"] if ptxas_info else []
 
+    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if not f.endswith(".cu")] + \
+        [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)]
+    hdr_mtime = max(os.path.getmtime(p) for p in headers)
+
     def compile_one(src):
         obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        # an object newer than its source and every header is reused (not with --force / --ptxas-info)
+        if (not force and not ptxas_info and os.path.exists(obj) and
+                os.path.getmtime(obj) >= max(os.path.getmtime(src), hdr_mtime)):
+            return obj
         cmd = [cc, *ARCH, *NVCC_FLAGS, *extra, "-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

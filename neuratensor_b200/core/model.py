@@ -8,11 +8,11 @@ initialisation order (embedding, blocks with attention interleaved, final
 norm, tied lm_head, then ``_init_weights``), so a seed gives the reference's
 weights and checkpoints load either way.
 
-The spike blocks run on the native kernels.  The glue around them
-(embedding gather, sliding-window attention, final RMSNorm, lm_head) stays
-in torch, as in the reference.  The forward collects every block's spike
-count in one device buffer and reads it once, instead of the reference's
-three host syncs per block.
+The spike blocks, the embedding gather, the sliding-window attention core
+and the final RMSNorm + tied lm_head (bf16 logits on the tcgen05 GEMM) run on
+the native kernels; the attention's RMSNorm and projections are torch ops.
+The forward collects every block's spike count in one device buffer and
+reads it once, instead of the reference's three host syncs per block.
 """
 from __future__ import annotations
 
@@ -247,7 +247,8 @@ class NeuraTensorModel(nn.Module):
 
     def _forward_rows(self, input_ids: Tensor, states: List[Optional[BlockState]], workspace: Optional[Tensor],
                       last_only: bool):
-        x = self.embedding(input_ids)
+        from .. import native
+        x = native.embedding(input_ids, self.embedding.weight)
         counts = torch.zeros(len(self.blocks), dtype=torch.int64, device=x.device)
         ws = workspace if workspace is not None else self._workspace(x)
         new_states: List[BlockState] = []
@@ -260,7 +261,9 @@ class NeuraTensorModel(nn.Module):
                     x = self.attn_layers[key](x)
             if last_only:
                 x = x[:, -1:]
-            logits = self.lm_head(self.norm(x))
+            # final RMSNorm + tied lm_head on the tcgen05 GEMM; the block
+            # workspace is free again here and holds the normalised rows
+            logits = native.lm_head(x, self.norm.weight, self.lm_head.weight, workspace=ws)
         return logits, new_states, counts
 
     def metrics_from_counts(self, counts: List[int], numel: int, dtype: torch.dtype) -> Dict:

@@ -310,6 +310,44 @@ int nt_rmsnorm_in_proj(int dtype, int64_t M, int64_t dm, int64_t di, const void*
 }
 
 // ---------------------------------------------------------------------------
+// Model glue: embedding gather, final RMSNorm + tied lm_head
+// ---------------------------------------------------------------------------
+int nt_embedding(int dtype, int64_t M, int64_t dm, int64_t vocab, const int64_t* ids, const void* W, void* out,
+                 void* stream) {
+    if (!act_dtype_ok(dtype)) return fail(NT_ERR_DTYPE, "nt_embedding: dtype %d", dtype);
+    if (M < 0 || dm < 1 || vocab < 1) return fail(NT_ERR_ARG, "nt_embedding: bad sizes");
+    if (M == 0) return NT_OK;
+    if (!ids || !W || !out) return fail(NT_ERR_ARG, "nt_embedding: null pointer");
+    return launch_embedding(dtype, M, dm, vocab, ids, W, out, as_stream(stream));
+}
+
+int64_t nt_lm_head_workspace_bytes(int dtype, int64_t M, int64_t dm, int64_t vocab) {
+    (void)vocab;
+    return align256(M * dm * esize(dtype));
+}
+
+int nt_lm_head(int dtype, int64_t M, int64_t dm, int64_t vocab, const void* x, const void* gamma, const void* W,
+               void* logits, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (!act_dtype_ok(dtype)) return fail(NT_ERR_DTYPE, "nt_lm_head: dtype %d", dtype);
+    if (M < 0 || dm < 1 || vocab < 1) return fail(NT_ERR_ARG, "nt_lm_head: bad sizes");
+    if (M == 0) return NT_OK;
+    if (!x || !gamma || !W || !logits) return fail(NT_ERR_ARG, "nt_lm_head: null pointer");
+    const int64_t need = nt_lm_head_workspace_bytes(dtype, M, dm, vocab);
+    if (!workspace || workspace_bytes < need)
+        return fail(NT_ERR_WORKSPACE, "nt_lm_head: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                    (long long)need);
+    NT_TRY(check_gemm_operand(workspace, dm, dtype, "nt_lm_head(x)"));
+    NT_TRY(check_gemm_operand(W, dm, dtype, "nt_lm_head(W)"));
+    cudaStream_t st = as_stream(stream);
+    NT_TRY(launch_rmsnorm(dtype, M, dm, x, gamma, workspace, st));
+    GemmArgs g{};
+    g.M = M; g.N = vocab; g.K = dm;
+    g.A = workspace; g.lda = dm; g.Bw = W; g.ldb = dm;
+    g.epi.kind = EPI_STORE; g.epi.out = logits; g.epi.ldo = vocab;
+    return launch_gemm(dtype, g, st);
+}
+
+// ---------------------------------------------------------------------------
 // FusedSpikeBlock.forward
 // ---------------------------------------------------------------------------
 int64_t nt_block_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N) {

@@ -59,6 +59,10 @@ int launch_lif_ssm_fused(const FusedArgs& a, cudaStream_t stream);
 int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w, void* y,
                    cudaStream_t stream);
 
+// Embedding rows out[r] = W[ids[r]] (ids outside [0, vocab): zero row and ERRF_BAD_ARG).
+int launch_embedding(int dtype, int64_t M, int64_t D, int64_t vocab, const int64_t* ids, const void* W, void* out,
+                     cudaStream_t stream);
+
 // Row compaction (the density decision of _sparse_out_proj): counters[0] =
 // n_active, counters[1] = 1 when the sparse branch is taken (2*n_active <= M),
 // counters[2] = rows the out_proj GEMM processes.  Only on the sparse branch

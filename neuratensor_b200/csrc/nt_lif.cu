@@ -306,6 +306,58 @@ lif_scan_kernel(LifArgs a, unsigned* err) {
     }
 }
 
+// Short sequences (T <= 32, e.g. decode steps): the tile ring above costs far
+// more than a few steps, so one thread owns one (batch, channel) membrane and
+// reads its inputs directly (consecutive channels: coalesced).  A 256-thread
+// CTA covers four 64-channel blocks of one batch row; each warp's ballot per
+// step gives the row-activity bit of its 32 channels, and the two warps of a
+// block combine their words through shared memory (T <= 32: one word).
+constexpr int kLifShortMaxT = 32;
+
+template <int DT, int MATH>
+__global__ void __launch_bounds__(256)
+lif_short_kernel(LifArgs a) {
+    using E = Elem<DT>;
+    using T = typename E::T;
+    using S = typename Elem<MATH>::T;
+    using M = MathOf<S>;
+    __shared__ unsigned s_bits[8];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t c = (int64_t)blockIdx.x * 256 + tid, b = blockIdx.y;
+    const bool live = c < a.C;
+    S beta = M::from(0.f), th = M::from(0.f), v = M::from(0.f);
+    if (live) {
+        beta = M::from(E::load(static_cast<const T*>(a.beta) + c));
+        th = M::from(E::load(static_cast<const T*>(a.threshold) + c));
+        if (a.mem_in) v = M::from(E::load(static_cast<const T*>(a.mem_in) + b * a.C + c));
+    }
+    const T* xb = static_cast<const T*>(a.x) + b * a.x_sb;
+    T* sb = static_cast<T*>(a.spikes) + b * a.s_sb;
+    unsigned bits = 0, count = 0;
+    for (int64_t t = 0; t < a.T; ++t) {
+        bool fired = false;
+        if (live) {
+            fired = lif_step(v, beta, th, M::in(xb[t * a.x_st + c]));
+            sb[t * a.s_st + c] = spike_val<T>(fired);
+        }
+        count += fired;
+        if (__ballot_sync(0xffffffffu, fired)) bits |= 1u << t;
+    }
+    if (live && a.mem_out) static_cast<T*>(a.mem_out)[b * a.C + c] = E::from_f(Elem<MATH>::to_f(v));
+    if (a.spike_count) {
+        const unsigned wsum = __reduce_add_sync(0xffffffffu, count);
+        if (lane == 0 && wsum) atomicAdd(a.spike_count, (unsigned long long)wsum);
+    }
+    if (a.row_bits) {
+        if (lane == 0) s_bits[warp] = bits;
+        __syncthreads();
+        // warps 2k and 2k+1 hold the 64 channels of block blockIdx.x*4 + k
+        const int64_t cblk = (int64_t)blockIdx.x * 4 + (tid >> 1);
+        if (tid < 4 && cblk * kLifChannels < a.C)
+            a.row_bits[(cblk * a.B + b) * a.n_words] = s_bits[2 * tid] | s_bits[2 * tid + 1];
+    }
+}
+
 }  // namespace
 
 template <int DT, int MATH>
@@ -317,6 +369,11 @@ int launch_lif_typed(const LifArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "lif_scan: smem attribute: %s", cudaGetErrorString(e));
     int dev = 0;
     cudaGetDevice(&dev);
+    if (a.T <= kLifShortMaxT) {
+        dim3 grid((unsigned)((a.C + 255) / 256), (unsigned)a.B);
+        lif_short_kernel<DT, MATH><<<grid, 256, 0, stream>>>(a);
+        return check_launch("lif_short_kernel");
+    }
     dim3 grid((unsigned)((a.C + kLifChannels - 1) / kLifChannels), (unsigned)a.B);
     kern<<<grid, kLifThreads, smem, stream>>>(a, device_error_word(dev));
     return check_launch("lif_scan_kernel");

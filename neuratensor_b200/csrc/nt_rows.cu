@@ -56,6 +56,51 @@ int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w
 }
 
 // ---------------------------------------------------------------------------
+// Embedding gather (model.py:258, nn.Embedding): out[r, :] = W[ids[r], :].
+// One warp per row, 16-byte vectors when rows allow.  An id outside
+// [0, vocab) writes a zero row and raises ERRF_BAD_ARG in the device error
+// word (the reference raises IndexError; a kernel reports instead of trapping).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) embedding_kernel(int64_t M, int64_t D, int64_t vocab, const int64_t* ids,
+                                                         const T* W, T* out, unsigned* err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const bool vec = ((D * (int64_t)sizeof(T)) % 16 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
+        const int64_t id = ids[r];
+        const bool ok = id >= 0 && id < vocab;
+        if (!ok && lane == 0 && err) atomicOr(err, ERRF_BAD_ARG);
+        T* o = out + r * D;
+        if (vec) {
+            const int64_t nv = D * (int64_t)sizeof(T) / 16;
+            const uint4* src = reinterpret_cast<const uint4*>(W + (ok ? id : 0) * D);
+            uint4* dst = reinterpret_cast<uint4*>(o);
+            for (int64_t i = lane; i < nv; i += 32) dst[i] = ok ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
+        } else {
+            for (int64_t i = lane; i < D; i += 32) o[i] = ok ? W[id * D + i] : T(0.f);
+        }
+    }
+}
+
+int launch_embedding(int dtype, int64_t M, int64_t D, int64_t vocab, const int64_t* ids, const void* W, void* out,
+                     cudaStream_t stream) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t blocks = std::min<int64_t>((M + 7) / 8, 148 * 16);
+    if (dtype == NT_F32)
+        embedding_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(M, D, vocab, ids, static_cast<const float*>(W),
+                                                                      static_cast<float*>(out), device_error_word(dev));
+    else if (dtype == NT_BF16)
+        embedding_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(
+            M, D, vocab, ids, static_cast<const __nv_bfloat16*>(W), static_cast<__nv_bfloat16*>(out),
+            device_error_word(dev));
+    else return fail(NT_ERR_DTYPE, "embedding: dtype %d", dtype);
+    return check_launch("embedding_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // flags[r] = any(spikes[r, :] != 0).  One warp per row, 16-byte loads when
 // the row is 16-byte aligned; a value is non-zero when its magnitude bits
 // are (so -0.0 counts as zero, as in torch's `any`).

@@ -92,47 +92,69 @@ __device__ __forceinline__ void static_for(F&& f) {
     }
 }
 
-// Shared-memory plan of one CTA: CPB channels of one batch row, 128 threads,
-// TPC threads per channel holding NPT states each (NP = TPC*NPT >= d_state).
-template <int TPC, int NPT, typename T>
+// Packed f32x2 arithmetic (sm_100 FFMA2 / FMUL2); NT_SCAN_SCALAR builds the same
+// arithmetic from scalar instructions (identical rounding) for comparison.
+__device__ __forceinline__ float2 pfma(float2 a, float2 b, float2 c) {
+#ifdef NT_SCAN_SCALAR
+    return make_float2(__fmaf_rn(a.x, b.x, c.x), __fmaf_rn(a.y, b.y, c.y));
+#else
+    return __ffma2_rn(a, b, c);
+#endif
+}
+__device__ __forceinline__ float2 pmul(float2 a, float2 b) {
+#ifdef NT_SCAN_SCALAR
+    return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+#else
+    return __fmul2_rn(a, b);
+#endif
+}
+
+// Shared-memory plan of one CTA: CPB = K*128/TPC channels of one batch row,
+// 128 threads, TPC threads per channel slice holding NPT states each (NP =
+// TPC*NPT >= d_state), K channels per thread.
+template <int TPC, int NPT, int K, typename T>
 struct ScanLayout {
     static constexpr int TCH = 32;                 // time steps per staged chunk
-    static constexpr int CPB = 128 / TPC;          // channels per CTA
+    static constexpr int SLOTS = 128 / TPC;        // channel slots per CTA
+    static constexpr int CPB = K * SLOTS;          // channels per CTA
     static constexpr int NP = TPC * NPT;           // padded d_state
     // raw staging (double-buffered): u|x, dt, gate tiles [TCH][CPB]; B, C tiles [TCH][NP]
     static constexpr int RAW = 3 * TCH * CPB + 2 * TCH * NP;
     static constexpr int RAW_BYTES = ((RAW * (int)sizeof(T)) + 15) & ~15;
-    // widened: (u, dt) [TCH][CPB] float2; B/(n+1) and C [TCH][NP] float each;
-    // output tile [TCH][CPB] of T; row positions [TCH]; 1/(n+1) [NP]
-    static constexpr int UD_BYTES = 8 * TCH * CPB;
-    static constexpr int BC_BYTES = 4 * 2 * TCH * NP;
+    // output tile [TCH][CPB] of T; row positions [TCH]; spike masks [CPB];
+    // general-path per-state constants [3][K][NPT/2][128] float2
     static constexpr int YO_BYTES = ((TCH * CPB * (int)sizeof(T)) + 15) & ~15;
-    static constexpr size_t BYTES = 2 * (size_t)RAW_BYTES + UD_BYTES + BC_BYTES + YO_BYTES + 4 * TCH + 4 * NP;
+    static constexpr size_t BYTES =
+        2 * (size_t)RAW_BYTES + YO_BYTES + 4 * TCH + 4 * CPB + 8 * 3 * K * (NPT / 2) * 128;
 };
 
-// Position of logical state n of a staged B or C row: the slices of the TPC
-// threads are interleaved by groups of four states (group q of every thread's
-// slice, then group q+1), so the 16-byte reads of one step by the threads of
-// a warp fall on consecutive bank groups (one wavefront for up to 8 slices;
-// threads of one slice read the same address, a broadcast).
-template <int TPC, int NPT>
-__device__ __forceinline__ int bc_pos(int n) {
-    const int sub = n / NPT, q = (n % NPT) >> 2;
-    return q * 4 * TPC + sub * 4 + (n & 3);
-}
-
-// Widen EPV = 16/sizeof(T) elements (one 16-byte vector) to float32.
-__device__ __forceinline__ void widen16(const float* src, float* v) {
-    const float4 q = *reinterpret_cast<const float4*>(src);
-    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
-}
-__device__ __forceinline__ void widen16(const __nv_bfloat16* src, float* v) {
-    const uint4 q = *reinterpret_cast<const uint4*>(src);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+// Load NPT consecutive elements of a staged row as floats (16-byte vector loads).
+template <int NPT>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[NPT]) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        v[2 * k] = __uint_as_float(w[k] << 16);
-        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    for (int q = 0; q < NPT / 8; ++q) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p + 8 * q);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[8 * q + 2 * i] = __uint_as_float(ww[i] << 16);
+            v[8 * q + 2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
+        }
+    }
+    if constexpr (NPT % 8 == 4) {
+        const uint2 w = *reinterpret_cast<const uint2*>(p + NPT - 4);
+        v[NPT - 4] = __uint_as_float(w.x << 16);
+        v[NPT - 3] = __uint_as_float(w.x & 0xffff0000u);
+        v[NPT - 2] = __uint_as_float(w.y << 16);
+        v[NPT - 1] = __uint_as_float(w.y & 0xffff0000u);
+    }
+}
+template <int NPT>
+__device__ __forceinline__ void load_row(const float* p, float (&v)[NPT]) {
+#pragma unroll
+    for (int q = 0; q < NPT / 4; ++q) {
+        const float4 w = *reinterpret_cast<const float4*>(p + 4 * q);
+        v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
     }
 }
 
@@ -162,33 +184,41 @@ __device__ __forceinline__ void reduce_scatter(float (&v)[TPC], int sub, unsigne
 // C, no outputs; writes the segment's end state (float32, from a zero start)
 // to state_out and its total decay exp(A*sum(dt)) per state to a.seg_decay.
 //
-// Thread (cl, sub) owns states [NPT*sub, NPT*sub + NPT) of channel c0 + cl.
-// Per chunk of TCH steps:
+// Thread (slot, sub) owns states [NPT*sub, NPT*sub + NPT) of the K channels
+// c0 + k*SLOTS + slot.  What bounds this kernel is shared memory: a warp's
+// 16-byte load costs four wavefronts even when its lanes share addresses, so
+// the cost of a step is the bytes each lane reads.  Each thread therefore
+// reads the staged raw tiles directly -- its slice of the step's B and C rows
+// (bf16: 16 bytes per 8 states, shared by its K channels) and u, dt of its
+// channels -- and derives everything else in registers: B/(n+1), and per
+// channel u/A0, dt*A0*log2(e), q = exp(dt*A0) and the decay chain.  In MODE 1
+// every thread of a channel runs that channel's LIF membrane itself (the same
+// arithmetic in each, so they agree), which keeps the chunk free of a serial
+// per-channel pass.  Per chunk of TCH steps:
 //   1. cp.async stages the next chunk's raw inputs while this one computes;
-//   2. one widening pass per CTA: (u, dt) per (step, channel) -- in MODE 1 one
-//      thread per channel runs the LIF membrane through the chunk here --
-//      and B/(n+1), C per (step, state), shared by every channel of the CTA;
-//   3. each thread advances its states through the chunk from registers, in
-//      groups of TPC steps whose partial C.h sums are combined by a register
-//      butterfly (reduce_scatter); the lane that ends up with step j's sum
-//      adds D*u, applies the gate and writes the output tile;
-//   4. the output tile goes to global memory with 16-byte stores.
-template <int DT, int SDT, int TPC, int NPT, int MODE, int OUT = 1>
-__global__ void __launch_bounds__(128, NPT == 8 ? 4 : 5)
+//   2. each thread advances its states through the chunk, in groups of TPC
+//      steps whose partial C.h sums are combined by a register butterfly
+//      (reduce_scatter); the sums stay in registers until the chunk is done;
+//   3. D*u, the gate and the rounding, into the output tile, which goes to
+//      global memory with 16-byte stores.
+#ifndef NT_SCAN_MINB8
+#define NT_SCAN_MINB8 3
+#endif
+template <int DT, int SDT, int TPC, int NPT, int K, int MODE, int OUT = 1>
+__global__ void __launch_bounds__(128, NPT == 8 ? NT_SCAN_MINB8 : 4)
 ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     static_assert(OUT == 1 || MODE == 0, "state-only pass is a MODE 0 variant");
     static_assert(NPT == 4 || NPT == 8, "4 or 8 states per thread");
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    using L = ScanLayout<TPC, NPT, T>;
-    constexpr int CPB = L::CPB, NP = L::NP, kTch = L::TCH, NPR = NPT / 2, NQ = NPT / 4;
+    using L = ScanLayout<TPC, NPT, K, T>;
+    constexpr int CPB = L::CPB, SLOTS = L::SLOTS, NP = L::NP, kTch = L::TCH, NPR = NPT / 2;
     constexpr int EPV = 16 / (int)sizeof(T);
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float2* w_ud = reinterpret_cast<float2*>(smem_raw + 2 * L::RAW_BYTES);            // [kTch][CPB] (u, dt)
-    float* w_B = reinterpret_cast<float*>(smem_raw + 2 * L::RAW_BYTES + L::UD_BYTES); // [kTch][NP] B/(n+1)
-    float* w_C = w_B + kTch * NP;                                                    // [kTch][NP] C
-    T* w_yo = reinterpret_cast<T*>(smem_raw + 2 * L::RAW_BYTES + L::UD_BYTES + L::BC_BYTES);  // [kTch][CPB]
-    int* w_pos = reinterpret_cast<int*>(smem_raw + 2 * L::RAW_BYTES + L::UD_BYTES + L::BC_BYTES + L::YO_BYTES);
-    float* w_rn = reinterpret_cast<float*>(w_pos + kTch);                            // [NP] 1/(n+1)
+    T* w_yo = reinterpret_cast<T*>(smem_raw + 2 * L::RAW_BYTES);                     // [kTch][CPB]
+    int* w_pos = reinterpret_cast<int*>(smem_raw + 2 * L::RAW_BYTES + L::YO_BYTES);  // [kTch]
+    unsigned* w_spk = reinterpret_cast<unsigned*>(w_pos + kTch);                     // [CPB] MODE 1 spike masks
+    // general path, per thread, channel and state pair: (A*log2e), ((n+1)/A), ((n+1) for |A| < 1e-6 else 0)
+    float2* w_gen = reinterpret_cast<float2*>(w_spk + CPB);                          // [3][K][NPR][128]
 
     const int64_t T_len = MODE ? f.L : a.T, d = MODE ? f.d : a.d, N = MODE ? f.N : a.N;
     const T* p_u = static_cast<const T*>(MODE ? f.x : a.u);
@@ -199,81 +229,102 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     const bool has_gate = p_g != nullptr;
     const int64_t ld_bc = (MODE == 0 && a.ld_bc > 0) ? a.ld_bc : N;
 
-    const int tid = threadIdx.x, cl = tid / TPC, sub = tid % TPC, lane = tid & 31;
+    const int tid = threadIdx.x, slot = tid / TPC, sub = tid % TPC, lane = tid & 31;
     const unsigned gmask = TPC >= 32 ? 0xffffffffu : (((1u << TPC) - 1u) << (lane & ~(TPC - 1)));
-    const int64_t c0 = (int64_t)blockIdx.x * CPB, c = c0 + cl, b = blockIdx.y;
-    const bool live = c < d;
+    const int64_t c0 = (int64_t)blockIdx.x * CPB, b = blockIdx.y;
+    auto chan = [&](int k) -> int64_t { return c0 + k * SLOTS + slot; };
 
-    // ---- per-state constants -------------------------------------------------
-    // A = -exp(log_A), rounded like the reference's own tensor op (ssm.py:121)
-    auto load_logA = [&](int64_t n) -> float {
-        if (MODE == 0) return Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.log_A) + c * N + n);
-        return f.log_A[c * N + n];
-    };
-    auto A_of = [&](float la) -> float { return MODE == 0 ? -Elem<DT>::rnd(expf(la)) : -expf(la); };
+    // ---- per-channel, per-state constants -------------------------------------
+    // A = -exp(log_A), rounded like the reference's own tensor op (ssm.py:121).
     // HiPPO structure test, per channel.  fp32 parameters: A[c,n] == (n+1)*A[c,0]
     // to 1e-6 relative.  bf16 parameters: log_A[c,n] == log(n+1) + log_A[c,0] to
     // one bf16 ulp of the stored value (the HiPPO init up to storage rounding).
     constexpr bool kBf16Params = (MODE == 0 && DT == NT_BF16);
-    float A2[NPT], h[NPT];
-    float2 ci2[NPR], lim2[NPR];
-    bool hippo_ok = true;
-    const float la0 = live ? load_logA(0) : 0.f;
-    const float Abase = live ? A_of(la0) : -1.f;
+    auto load_logA = [&](int64_t c, int64_t n) -> float {
+        if (MODE == 0) return Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.log_A) + c * N + n);
+        return f.log_A[c * N + n];
+    };
+    auto A_of = [&](float la) -> float { return MODE == 0 ? -Elem<DT>::rnd(expf(la)) : -expf(la); };
     const void* sin = MODE ? (const void*)f.state_in : a.state_in;
+    float2 hv[K][NPR];                               // the thread's states, as packed pairs
+    float a0l[K], ra0[K], Dv[K];
+    bool live[K], hippo[K];
 #pragma unroll
-    for (int j = 0; j < NPT; ++j) {
-        const int64_t n = (int64_t)sub * NPT + j;
-        float A = 0.f;
-        h[j] = 0.f;
-        const bool on = live && n < N;
-        if (on) {
-            const float la = load_logA(n);
-            A = A_of(la);
-            if (sin) {
-                const int64_t si = (b * d + c) * N + n;
-                if (MODE == 0 && SDT == NT_BF16) h[j] = __bfloat162float(static_cast<const __nv_bfloat16*>(sin)[si]);
-                else h[j] = static_cast<const float*>(sin)[si];
+    for (int k = 0; k < K; ++k) {
+        const int64_t c = chan(k);
+        live[k] = c < d;
+        bool ok = true;
+        const float la0 = live[k] ? load_logA(c, 0) : 0.f;
+        const float Abase = live[k] ? A_of(la0) : -1.f;
+        a0l[k] = Abase * kLog2e;
+        ra0[k] = 1.0f / Abase;
+        Dv[k] = 0.f;
+        if (live[k]) Dv[k] = MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + c) : f.Dskip[c];
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int64_t n = (int64_t)sub * NPT + j;
+            float A = 0.f, h0 = 0.f;
+            const bool on = live[k] && n < N;
+            if (on) {
+                const float la = load_logA(c, n);
+                A = A_of(la);
+                if (sin) {
+                    const int64_t si = (b * d + c) * N + n;
+                    if (MODE == 0 && SDT == NT_BF16) h0 = __bfloat162float(static_cast<const __nv_bfloat16*>(sin)[si]);
+                    else h0 = static_cast<const float*>(sin)[si];
+                }
+                if (kBf16Params) {
+                    int e2;
+                    frexpf(la, &e2);                               // |la| in [2^(e2-1), 2^e2)
+                    const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
+                    if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) ok = false;
+                } else if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) {
+                    ok = false;
+                }
             }
-            if (kBf16Params) {
-                int e2;
-                frexpf(la, &e2);                                   // |la| in [2^(e2-1), 2^e2)
-                const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
-                if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) hippo_ok = false;
-            } else if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) {
-                hippo_ok = false;
-            }
+            const bool lim = on && fabsf(A) < 1e-6f;
+            if (lim) ok = false;
+            // general path on B' = B/(n+1): B_bar*u = (A_bar - 1) * ((n+1)/A) * B' * u,
+            // or dt * (n+1) * B' * u for the |A| < 1e-6 states (ssm.py:129-137)
+            const float np1 = (float)(n + 1);
+            const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
+            const int gi = ((0 * K + k) * NPR + j / 2) * 128 + tid, gs = K * NPR * 128;
+            reinterpret_cast<float*>(w_gen + gi)[j & 1] = A * kLog2e;
+            reinterpret_cast<float*>(w_gen + gi + gs)[j & 1] = ci;
+            reinterpret_cast<float*>(w_gen + gi + 2 * gs)[j & 1] = lim ? np1 : 0.f;
+            if (j & 1) hv[k][j / 2].y = h0;
+            else hv[k][j / 2].x = h0;
         }
-        const bool lim = on && fabsf(A) < 1e-6f;
-        if (lim) hippo_ok = false;
-        A2[j] = A * kLog2e;
-        // general path on B' = B/(n+1): B_bar*u = (A_bar - 1) * ((n+1)/A) * B' * u,
-        // or dt * (n+1) * B' * u for the |A| < 1e-6 states (ssm.py:129-137)
-        const float np1 = (float)(n + 1);
-        const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
-        if (j & 1) { ci2[j / 2].y = ci; lim2[j / 2].y = lim ? np1 : 0.f; }
-        else { ci2[j / 2].x = ci; lim2[j / 2].x = lim ? np1 : 0.f; }
+        // one decision per channel: every state of the channel must qualify
+        const unsigned okm = __ballot_sync(0xffffffffu, ok);
+        hippo[k] = (okm & gmask) == gmask;
     }
-    // one decision per channel: every state of the channel must qualify
-    const unsigned okm = __ballot_sync(0xffffffffu, hippo_ok);
-    const bool hippo = (okm & gmask) == gmask;
-    // HiPPO constants: first-state exponent, ratio exponent, 1/A[c,0]
-    const float a2first = (float)(sub * NPT + 1) * Abase * kLog2e;
-    const float q2 = Abase * kLog2e;
-    const float rA0 = 1.0f / Abase;
-    float Dv = 0.f;
-    if (live) Dv = MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + c) : f.Dskip[c];
+    bool all_hippo = true;
+#pragma unroll
+    for (int k = 0; k < K; ++k) all_hippo = all_hippo && hippo[k];
+    // the HiPPO path needs every channel of the thread to qualify (else the
+    // general path, which is exact for any A, runs for all of them)
+    const bool use_hippo = all_hippo;
+    float rn[NPT];                                   // 1/(n+1) of the thread's states
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) rn[j] = 1.0f / (float)(sub * NPT + j + 1);
+    // HiPPO: exponents of the thread's first two states, (n0+1) and (n0+2) times dt*A0*log2(e)
+    const float np1a = (float)(sub * NPT + 1), np1b = (float)(sub * NPT + 2);
 
-    float beta = 0.f, th = 0.f, mem = 0.f;          // MODE 1: thread tid < CPB runs channel c0 + tid's LIF
-    const int64_t cm = c0 + tid;
-    if (MODE == 1 && tid < CPB && cm < d) {
-        beta = f.beta[cm];
-        th = f.threshold[cm];
-        if (f.mem_in) mem = f.mem_in[b * d + cm];
+    float beta[K], th[K], mem[K];                    // MODE 1: every thread of a channel runs its LIF
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        beta[k] = th[k] = mem[k] = 0.f;
+        if (MODE == 1 && live[k]) {
+            beta[k] = f.beta[chan(k)];
+            th[k] = f.threshold[chan(k)];
+            if (f.mem_in) mem[k] = f.mem_in[b * d + chan(k)];
+        }
     }
     unsigned spike_local = 0;
-    float dt_sum = 0.f;                             // state-only pass: sum of dt over the segment
-    for (int i = tid; i < NP; i += 128) w_rn[i] = 1.0f / (float)(i + 1);
+    float dt_sum[K];                                 // state-only pass: sum of dt over the segment
+#pragma unroll
+    for (int k = 0; k < K; ++k) dt_sum[k] = 0.f;
     const bool sparse_rows = (MODE == 0) && a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
 
     // 16-byte staging is possible when every tile row starts 16-byte aligned
@@ -284,7 +335,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                         ((reinterpret_cast<uintptr_t>(p_B) | reinterpret_cast<uintptr_t>(p_C)) & 15) == 0;
     const int64_t row0 = b * T_len;   // first (batch, time) row of this batch element
 
-    auto raw_buf = [&](int k) { return reinterpret_cast<T*>(smem_raw + (k & 1) * L::RAW_BYTES); };
+    auto raw_buf = [&](int kk) { return reinterpret_cast<T*>(smem_raw + (kk & 1) * L::RAW_BYTES); };
     auto issue = [&](int64_t t0, T* rb) {
         T* r_u = rb;
         T* r_dt = r_u + kTch * CPB;
@@ -299,73 +350,6 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         cp_async_commit();
     };
 
-    // One step of this thread's NPT states.  Steps past the end of the
-    // sequence see u = dt = B = 0, which leaves the state unchanged.
-    auto step = [&](int tt, auto hip) -> float {
-        constexpr bool HIP = decltype(hip)::value;
-        float Bf[NPT], Cf[NPT];
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-            const int o = tt * NP + q * 4 * TPC + sub * 4;
-            const float4 bq = *reinterpret_cast<const float4*>(w_B + o);
-            Bf[4 * q] = bq.x; Bf[4 * q + 1] = bq.y; Bf[4 * q + 2] = bq.z; Bf[4 * q + 3] = bq.w;
-            if (OUT) {
-                const float4 cq = *reinterpret_cast<const float4*>(w_C + o);
-                Cf[4 * q] = cq.x; Cf[4 * q + 1] = cq.y; Cf[4 * q + 2] = cq.z; Cf[4 * q + 3] = cq.w;
-            }
-        }
-        const float2 ud = w_ud[tt * CPB + cl];
-        const float u = ud.x, dtv = ud.y;
-        float2 av[NPR], hv[NPR];
-#pragma unroll
-        for (int j = 0; j < NPR; ++j) hv[j] = make_float2(h[2 * j], h[2 * j + 1]);
-        if (HIP) {
-            // A[n] = (n+1) A0.  With e = A_bar - 1 = exp(dt A[n]) - 1 and
-            // w = u B/((n+1) A0) = u B_bar / e, the update A_bar h + B_bar u is
-            //     h' = h + e (h + w)      (two fmas: t = B' * u/A0 + h, h + e t)
-            // and e follows the chain e[n+1] = e[n] q + (q - 1), q = exp(dt A0).
-            const float e0 = ex2(dtv * a2first) - 1.0f;
-            const float qv = ex2(dtv * q2);
-            av[0] = make_float2(e0, __fmaf_rn(e0, qv, qv - 1.0f));
-            const float qs = qv * qv;
-            const float2 qq = make_float2(qs, qs);
-            const float qm = __fmaf_rn(qv, qv, -1.0f);
-            const float2 qqm = make_float2(qm, qm);
-#pragma unroll
-            for (int j = 1; j < NPR; ++j) av[j] = __ffma2_rn(av[j - 1], qq, qqm);
-            const float sc = u * rA0;
-            const float2 ss = make_float2(sc, sc);
-#pragma unroll
-            for (int j = 0; j < NPR; ++j) {
-                const float2 t = __ffma2_rn(make_float2(Bf[2 * j], Bf[2 * j + 1]), ss, hv[j]);
-                hv[j] = __ffma2_rn(av[j], t, hv[j]);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < NPR; ++j) av[j] = make_float2(ex2(dtv * A2[2 * j]), ex2(dtv * A2[2 * j + 1]));
-            const float2 uu = make_float2(u, u), dd = make_float2(dtv, dtv);
-#pragma unroll
-            for (int j = 0; j < NPR; ++j) {
-                const float2 nci = make_float2(-ci2[j].x, -ci2[j].y);
-                const float2 coef = __ffma2_rn(dd, lim2[j], __ffma2_rn(av[j], ci2[j], nci));
-                const float2 bu = __fmul2_rn(coef, __fmul2_rn(make_float2(Bf[2 * j], Bf[2 * j + 1]), uu));
-                hv[j] = __ffma2_rn(av[j], hv[j], bu);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < NPR; ++j) { h[2 * j] = hv[j].x; h[2 * j + 1] = hv[j].y; }
-        if constexpr (OUT) {
-            // C.h as one packed fma chain, then one add of the two lanes
-            float2 y2 = __fmul2_rn(make_float2(Cf[0], Cf[1]), hv[0]);
-#pragma unroll
-            for (int j = 1; j < NPR; ++j) y2 = __ffma2_rn(make_float2(Cf[2 * j], Cf[2 * j + 1]), hv[j], y2);
-            return y2.x + y2.y;
-        } else {
-            dt_sum += dtv;                         // the segment's total decay exponent
-            return 0.f;
-        }
-    };
-
     const int nchunks = (int)((T_len + kTch - 1) / kTch);
     issue(0, raw_buf(0));
     for (int kc = 0; kc < nchunks; ++kc) {
@@ -376,91 +360,143 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         } else {
             cp_async_wait<0>();
         }
+        if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
         __syncthreads();
         const int nt = (T_len - t0 < kTch) ? (int)(T_len - t0) : kTch;
-        // ---- widening pass --------------------------------------------------
         const T* rb = raw_buf(kc);
         const T* r_u = rb;
         const T* r_dt = r_u + kTch * CPB;
         const T* r_g = r_dt + kTch * CPB;
         const T* r_B = r_g + kTch * CPB;
         const T* r_C = r_B + kTch * NP;
-        if (MODE == 0) {
-            for (int i = tid * EPV; i < kTch * CPB; i += 128 * EPV) {
-                float uv[EPV], dv[EPV];
-                widen16(r_u + i, uv);
-                widen16(r_dt + i, dv);
+        unsigned smask[K];                           // MODE 1: this chunk's spikes, bit tt
 #pragma unroll
-                for (int k = 0; k < EPV; k += 2)
-                    *reinterpret_cast<float4*>(w_ud + i + k) = make_float4(uv[k], dv[k], uv[k + 1], dv[k + 1]);
-            }
-        } else if (tid < CPB) {
-            // LIF (snn.py:177-181) in fp32 for channel c0 + tid through the chunk;
-            // steps past the sequence end give u = 0 and leave the membrane alone
-            const bool on = cm < d;
-#pragma unroll 4
-            for (int tt = 0; tt < kTch; ++tt) {
-                const float xv = to_f(r_u[tt * CPB + tid]);
-                const float m1 = __fadd_rn(__fmul_rn(beta, mem), xv);
-                const float s1 = (m1 >= th) ? 1.f : 0.f;
-                const bool in_seq = on && tt < nt;
-                const float uu = in_seq ? s1 : 0.f;
-                mem = in_seq ? __fsub_rn(m1, __fmul_rn(th, s1)) : mem;
-                w_ud[tt * CPB + tid] = make_float2(uu, to_f(r_dt[tt * CPB + tid]));
-                if (in_seq) {
-                    spike_local += uu != 0.f;
-                    if (f.spikes) {
-                        const int64_t idx = (row0 + t0 + tt) * d + cm;
-                        if (f.spike_dtype == NT_U8) static_cast<unsigned char*>(f.spikes)[idx] = (unsigned char)(uu != 0.f);
-                        else static_cast<__nv_bfloat16*>(f.spikes)[idx] = __float2bfloat16_rn(uu);
+        for (int k = 0; k < K; ++k) smask[k] = 0;
+
+        // One step of this thread's K x NPT states; returns the K partial C.h
+        // sums.  Steps past the end of the sequence see u = dt = B = 0, which
+        // leaves the state unchanged.
+        auto step = [&](int tt, auto hip, float (&yk)[K]) {
+            constexpr bool HIP = decltype(hip)::value;
+            float Bv[NPT], Cv[NPT];
+            load_row<NPT>(r_B + tt * NP + sub * NPT, Bv);
+            if (OUT) load_row<NPT>(r_C + tt * NP + sub * NPT, Cv);
+            float2 Bp[NPR];
+#pragma unroll
+            for (int j = 0; j < NPR; ++j)
+                Bp[j] = pmul(make_float2(Bv[2 * j], Bv[2 * j + 1]), make_float2(rn[2 * j], rn[2 * j + 1]));
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int cc = k * SLOTS + slot;
+                float u;
+                const float dtv = to_f(r_dt[tt * CPB + cc]);
+                if (MODE == 0) {
+                    u = to_f(r_u[tt * CPB + cc]);
+                } else {
+                    // LIF step (snn.py:177-181) in fp32
+                    const float m1 = __fadd_rn(__fmul_rn(beta[k], mem[k]), to_f(r_u[tt * CPB + cc]));
+                    const float s1 = (m1 >= th[k]) ? 1.f : 0.f;
+                    const bool in_seq = live[k] && tt < nt;
+                    u = in_seq ? s1 : 0.f;
+                    mem[k] = in_seq ? __fsub_rn(m1, __fmul_rn(th[k], s1)) : mem[k];
+                    smask[k] |= (u != 0.f ? 1u : 0u) << tt;
+                }
+                float2 av[NPR];
+                if (HIP) {
+                    // A[n] = (n+1) A0.  With e = A_bar - 1 = exp(dt A[n]) - 1 and
+                    // w = u B/((n+1) A0) = u B_bar / e, the update A_bar h + B_bar u is
+                    //     h' = h + e (h + w)      (two fmas: t = B' * u/A0 + h, h + e t)
+                    // and e follows the chain e[n+2] = e[n] q^2 + (q^2 - 1), q = exp(dt A0),
+                    // seeded by the exponentials of the thread's first two states.
+                    const float x0 = dtv * a0l[k], s = u * ra0[k];
+                    const float q = ex2(x0);
+                    const float qs = q * q, qm = __fmaf_rn(q, q, -1.0f);
+                    av[0] = make_float2(ex2(x0 * np1a) - 1.0f, ex2(x0 * np1b) - 1.0f);
+                    const float2 qq = make_float2(qs, qs), qqm = make_float2(qm, qm), ss = make_float2(s, s);
+#pragma unroll
+                    for (int j = 1; j < NPR; ++j) av[j] = pfma(av[j - 1], qq, qqm);
+#pragma unroll
+                    for (int j = 0; j < NPR; ++j) hv[k][j] = pfma(av[j], pfma(Bp[j], ss, hv[k][j]), hv[k][j]);
+                } else {
+                    const float2 uu = make_float2(u, u), dd = make_float2(dtv, dtv);
+                    constexpr int gs = K * NPR * 128;
+#pragma unroll
+                    for (int j = 0; j < NPR; ++j) {
+                        const int gi = (k * NPR + j) * 128 + tid;
+                        const float2 A2 = w_gen[gi], ci = w_gen[gi + gs], lm = w_gen[gi + 2 * gs];
+                        av[j] = make_float2(ex2(dtv * A2.x), ex2(dtv * A2.y));
+                        const float2 coef = pfma(dd, lm, pfma(av[j], ci, make_float2(-ci.x, -ci.y)));
+                        hv[k][j] = pfma(av[j], hv[k][j], pmul(coef, pmul(Bp[j], uu)));
                     }
                 }
-            }
-        }
-        for (int i = tid * EPV; i < kTch * NP; i += 128 * EPV) {
-            float bv[EPV], cv[EPV];
-            widen16(r_B + i, bv);
-            if (OUT) widen16(r_C + i, cv);
-#pragma unroll
-            for (int k = 0; k < EPV; k += 4) {
-                const int tt = (i + k) / NP, n = (i + k) % NP;     // four states of one row
-                const int o = tt * NP + bc_pos<TPC, NPT>(n);
-                const float4 r4 = *reinterpret_cast<const float4*>(w_rn + n);
-                *reinterpret_cast<float4*>(w_B + o) =
-                    make_float4(bv[k] * r4.x, bv[k + 1] * r4.y, bv[k + 2] * r4.z, bv[k + 3] * r4.w);
-                if (OUT) *reinterpret_cast<float4*>(w_C + o) = make_float4(cv[k], cv[k + 1], cv[k + 2], cv[k + 3]);
-            }
-        }
-        if (sparse_rows && tid < kTch) w_pos[tid] = (t0 + tid < T_len) ? a.row_pos[row0 + t0 + tid] : -1;
-        __syncthreads();
-        // ---- recurrence: groups of TPC steps, partial sums combined in registers
-        auto run = [&](auto hip) {
-            static_for<0, kTch / TPC>([&](auto grp) {
-                constexpr int g0 = decltype(grp)::value * TPC;
-                float yp[TPC];
-                static_for<0, TPC>([&](auto j) { yp[decltype(j)::value] = step(g0 + decltype(j)::value, hip); });
                 if constexpr (OUT) {
-                    if constexpr (TPC > 1) reduce_scatter<TPC>(yp, sub, gmask);
-                    const int tt = g0 + (TPC > 1 ? sub : 0);
-                    const float uu = w_ud[tt * CPB + cl].x;
-                    const float yv = __fadd_rn(yp[0], __fmul_rn(Dv, uu));
-                    if (MODE == 0) {
-                        using E = Elem<DT>;
-                        float o = E::rnd(yv);
-                        if (has_gate) {
-                            const float gv = to_f(r_g[tt * CPB + cl]);
-                            o = E::rnd(o * (a.gate_is_silu ? gv : E::rnd(silu_f(gv))));
-                        }
-                        w_yo[tt * CPB + cl] = E::from_f(o);
-                    } else {
-                        w_yo[tt * CPB + cl] = __float2bfloat16_rn(yv);
+                    // C.h as two packed fma chains (halving the dependent depth), then the lanes
+                    float2 ya = pmul(make_float2(Cv[0], Cv[1]), hv[k][0]);
+                    float2 yb = pmul(make_float2(Cv[2], Cv[3]), hv[k][1]);
+#pragma unroll
+                    for (int j = 2; j < NPR; j += 2) {
+                        ya = pfma(make_float2(Cv[2 * j], Cv[2 * j + 1]), hv[k][j], ya);
+                        yb = pfma(make_float2(Cv[2 * j + 2], Cv[2 * j + 3]), hv[k][j + 1], yb);
+                    }
+                    yk[k] = (ya.x + yb.x) + (ya.y + yb.y);
+                } else {
+                    dt_sum[k] += dtv;                  // the segment's total decay exponent
+                    yk[k] = 0.f;
+                }
+            }
+        };
+        // ---- recurrence: groups of TPC steps, partial sums combined in registers
+        constexpr int NG = kTch / TPC;
+        float yfin[K][NG];
+        auto run = [&](auto hip) {
+            static_for<0, NG>([&](auto grp) {
+                constexpr int g = decltype(grp)::value;
+                float yp[K][TPC];
+                static_for<0, TPC>([&](auto j) {
+                    float yk[K];
+                    step(g * TPC + decltype(j)::value, hip, yk);
+#pragma unroll
+                    for (int k = 0; k < K; ++k) yp[k][decltype(j)::value] = yk[k];
+                });
+                if constexpr (OUT) {
+#pragma unroll
+                    for (int k = 0; k < K; ++k) {
+                        if constexpr (TPC > 1) reduce_scatter<TPC>(yp[k], sub, gmask);
+                        yfin[k][g] = yp[k][0];
                     }
                 }
             });
         };
-        if (hippo) run(std::true_type{});
+        if (use_hippo) run(std::true_type{});
         else run(std::false_type{});
         if constexpr (OUT) {
+            // D*u, the gate and the rounding (thread (slot, sub) holds step g*TPC + sub
+            // of each of its channels for every group g)
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int cc = k * SLOTS + slot;
+#pragma unroll
+                for (int g = 0; g < NG; ++g) {
+                    const int tt = g * TPC + (TPC > 1 ? sub : 0);
+                    const float uu = MODE == 0 ? to_f(r_u[tt * CPB + cc]) : (float)((smask[k] >> tt) & 1u);
+                    const float yv = __fadd_rn(yfin[k][g], __fmul_rn(Dv[k], uu));
+                    if constexpr (MODE == 0) {
+                        using E = Elem<DT>;
+                        float o = E::rnd(yv);
+                        if (has_gate) {
+                            const float gv = to_f(r_g[tt * CPB + cc]);
+                            o = E::rnd(o * (a.gate_is_silu ? gv : E::rnd(silu_f(gv))));
+                        }
+                        w_yo[tt * CPB + cc] = E::from_f(o);
+                    } else {
+                        w_yo[tt * CPB + cc] = __float2bfloat16_rn(yv);
+                    }
+                }
+                if (MODE == 1 && sub == 0) {
+                    w_spk[cc] = smask[k];
+                    spike_local += __popc(smask[k]);
+                }
+            }
             __syncthreads();
             // ---- output tile -> global (16-byte stores where rows allow) -------
             constexpr int VPR = (CPB * (int)sizeof(T)) % 16 == 0 ? CPB * (int)sizeof(T) / 16 : 1;
@@ -492,42 +528,56 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
                     p_y[row * d + c0 + cc] = w_yo[tt * CPB + cc];
                 }
             }
+            if (MODE == 1 && f.spikes) {
+                // the chunk's spikes, one byte (or bf16) per (step, channel), consecutive channels per thread
+                for (int i = tid; i < kTch * CPB; i += 128) {
+                    const int tt = i / CPB, cc = i % CPB;
+                    if (tt >= nt || c0 + cc >= d) continue;
+                    const unsigned sbit = (w_spk[cc] >> tt) & 1u;
+                    const int64_t idx = (row0 + t0 + tt) * d + c0 + cc;
+                    if (f.spike_dtype == NT_U8) static_cast<unsigned char*>(f.spikes)[idx] = (unsigned char)sbit;
+                    else static_cast<__nv_bfloat16*>(f.spikes)[idx] = __float2bfloat16_rn((float)sbit);
+                }
+            }
         }
         __syncthreads();   // raw_buf(kc) and the tiles are refilled by the next chunk
     }
     // ---- carry-out -----------------------------------------------------------
-    if constexpr (!OUT) {
-        // end state of the segment (float32) and its decay exp(A*sum(dt)) per state
-        if (live) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int64_t c = chan(k);
+        if (!live[k]) continue;
+        if constexpr (!OUT) {
+            // end state of the segment (float32) and its decay exp(A*sum(dt)) per state
 #pragma unroll
             for (int j = 0; j < NPT; ++j) {
                 const int64_t n = (int64_t)sub * NPT + j;
                 if (n >= N) continue;
                 const int64_t si = (b * d + c) * N + n;
-                const float a2 = hippo ? (float)(n + 1) * Abase * kLog2e : A2[j];
-                static_cast<float*>(a.state_out)[si] = h[j];
-                a.seg_decay[si] = ex2(a2 * dt_sum);
+                const float2 A2 = w_gen[(k * NPR + j / 2) * 128 + tid];
+                const float a2 = use_hippo ? (float)(n + 1) * a0l[k] : ((j & 1) ? A2.y : A2.x);
+                static_cast<float*>(a.state_out)[si] = (j & 1) ? hv[k][j / 2].y : hv[k][j / 2].x;
+                a.seg_decay[si] = ex2(a2 * dt_sum[k]);
             }
-        }
-        return;
-    }
-    void* sout = MODE ? (void*)f.state_out : a.state_out;
-    if (live && sout) {
+        } else {
+            void* sout = MODE ? (void*)f.state_out : a.state_out;
+            if (sout) {
 #pragma unroll
-        for (int j = 0; j < NPT; ++j) {
-            const int64_t n = (int64_t)sub * NPT + j;
-            if (n >= N) continue;
-            const int64_t si = (b * d + c) * N + n;
-            if (MODE == 0 && SDT == NT_BF16) static_cast<__nv_bfloat16*>(sout)[si] = __float2bfloat16_rn(h[j]);
-            else static_cast<float*>(sout)[si] = h[j];
+                for (int j = 0; j < NPT; ++j) {
+                    const int64_t n = (int64_t)sub * NPT + j;
+                    if (n >= N) continue;
+                    const int64_t si = (b * d + c) * N + n;
+                    const float hj = (j & 1) ? hv[k][j / 2].y : hv[k][j / 2].x;
+                    if (MODE == 0 && SDT == NT_BF16) static_cast<__nv_bfloat16*>(sout)[si] = __float2bfloat16_rn(hj);
+                    else static_cast<float*>(sout)[si] = hj;
+                }
+            }
+            if (MODE == 1 && sub == 0 && f.mem_out) f.mem_out[b * d + c] = mem[k];
         }
     }
-    if (MODE == 1) {
-        if (tid < CPB && cm < d && f.mem_out) f.mem_out[b * d + cm] = mem;
-        if (f.spike_count) {
-            const unsigned w = __reduce_add_sync(0xffffffffu, spike_local);
-            if ((tid & 31) == 0 && w) atomicAdd(f.spike_count, (unsigned long long)w);
-        }
+    if (MODE == 1 && f.spike_count) {
+        const unsigned w = __reduce_add_sync(0xffffffffu, spike_local);
+        if ((tid & 31) == 0 && w) atomicAdd(f.spike_count, (unsigned long long)w);
     }
 }
 
@@ -537,11 +587,11 @@ int pow2_at_least(int64_t x) {
     return p;
 }
 
-template <int DT, int SDT, int MODE, int TPC, int NPT, int OUT>
+template <int DT, int SDT, int MODE, int TPC, int NPT, int K, int OUT>
 int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     using T = typename Elem<MODE == 0 ? DT : NT_BF16>::T;
-    using L = ScanLayout<TPC, NPT, T>;
-    auto kern = ssm_scan_kernel<DT, SDT, TPC, NPT, MODE, OUT>;
+    using L = ScanLayout<TPC, NPT, K, T>;
+    auto kern = ssm_scan_kernel<DT, SDT, TPC, NPT, K, MODE, OUT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES);
     if (e != cudaSuccess) return fail(NT_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
     const int64_t d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
@@ -550,87 +600,96 @@ int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     return check_launch("ssm_scan_kernel");
 }
 
-#ifndef NT_SCAN_NARROW_WARPS
-#define NT_SCAN_NARROW_WARPS 3
+#ifndef NT_SCAN_WIDE_WARPS
+#define NT_SCAN_WIDE_WARPS 6
 #endif
-// States per thread: 8, or 4 when 8 would give the GPU fewer than
-// NT_SCAN_NARROW_WARPS warps per SM sub-partition: the recurrence of one warp
-// is a serial chain over T, so a sub-partition with one warp more than its
-// neighbours sets the kernel's time, and halving the slice doubles the warps.
+// Slicing: 8 states per thread (TPC = N/8 threads per channel).  Two channels
+// per thread (their B and C slices loaded once) when that still leaves every
+// SM sub-partition NT_SCAN_WIDE_WARPS warps or more: the recurrence of one
+// warp is a serial chain over T, so warps per sub-partition, and how evenly
+// they divide, set the time when the batch is small.
 template <int DT, int SDT, int MODE, int OUT = 1>
 int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     const int64_t N = MODE ? f.N : a.N, d = MODE ? f.d : a.d, B = MODE ? f.B : a.B;
     if (N > 256) return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)N);
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int tpc8 = pow2_at_least((N + 7) / 8);
-    const int64_t warps8 = B * ((d + 128 / tpc8 - 1) / (128 / tpc8)) * 4;
-    const bool narrow = N > 4 && tpc8 <= 16 && warps8 < (int64_t)NT_SCAN_NARROW_WARPS * 4 * sms;
-    if (narrow || N <= 4) {
-        switch (pow2_at_least((N + 3) / 4)) {
-            case 1: return launch_tpc<DT, SDT, MODE, 1, 4, OUT>(a, f, stream);
-            case 2: return launch_tpc<DT, SDT, MODE, 2, 4, OUT>(a, f, stream);
-            case 4: return launch_tpc<DT, SDT, MODE, 4, 4, OUT>(a, f, stream);
-            case 8: return launch_tpc<DT, SDT, MODE, 8, 4, OUT>(a, f, stream);
-            case 16: return launch_tpc<DT, SDT, MODE, 16, 4, OUT>(a, f, stream);
-            case 32: return launch_tpc<DT, SDT, MODE, 32, 4, OUT>(a, f, stream);
+    const int tpc = pow2_at_least((N + 7) / 8);
+    const int64_t warps2 = B * ((d + 2 * 128 / tpc - 1) / (2 * 128 / tpc)) * 4;
+    // (bf16 inputs only: the float32 path is the parity configuration)
+    const bool wide = (MODE == 1 || DT == NT_BF16) && OUT == 1 && tpc <= 16 &&
+                      warps2 >= (int64_t)NT_SCAN_WIDE_WARPS * 4 * sms;
+    if constexpr (MODE == 1 || (DT == NT_BF16 && OUT == 1)) {
+      if (wide) {
+        switch (tpc) {
+            case 1: return launch_tpc<DT, SDT, MODE, 1, 8, 2, OUT>(a, f, stream);
+            case 2: return launch_tpc<DT, SDT, MODE, 2, 8, 2, OUT>(a, f, stream);
+            case 4: return launch_tpc<DT, SDT, MODE, 4, 8, 2, OUT>(a, f, stream);
+            case 8: return launch_tpc<DT, SDT, MODE, 8, 8, 2, OUT>(a, f, stream);
+            case 16: return launch_tpc<DT, SDT, MODE, 16, 8, 2, OUT>(a, f, stream);
             default: break;
         }
+      }
     }
-    switch (tpc8) {
-        case 1: return launch_tpc<DT, SDT, MODE, 1, 8, OUT>(a, f, stream);
-        case 2: return launch_tpc<DT, SDT, MODE, 2, 8, OUT>(a, f, stream);
-        case 4: return launch_tpc<DT, SDT, MODE, 4, 8, OUT>(a, f, stream);
-        case 8: return launch_tpc<DT, SDT, MODE, 8, 8, OUT>(a, f, stream);
-        case 16: return launch_tpc<DT, SDT, MODE, 16, 8, OUT>(a, f, stream);
-        case 32: return launch_tpc<DT, SDT, MODE, 32, 8, OUT>(a, f, stream);
+    switch (tpc) {
+        case 1: return launch_tpc<DT, SDT, MODE, 1, 8, 1, OUT>(a, f, stream);
+        case 2: return launch_tpc<DT, SDT, MODE, 2, 8, 1, OUT>(a, f, stream);
+        case 4: return launch_tpc<DT, SDT, MODE, 4, 8, 1, OUT>(a, f, stream);
+        case 8: return launch_tpc<DT, SDT, MODE, 8, 8, 1, OUT>(a, f, stream);
+        case 16: return launch_tpc<DT, SDT, MODE, 16, 8, 1, OUT>(a, f, stream);
+        case 32: return launch_tpc<DT, SDT, MODE, 32, 8, 1, OUT>(a, f, stream);
         default: return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)N);
     }
 }
 
 // ---------------------------------------------------------------------------
-// Short sequences (decode steps, T <= kStepMaxT): one warp per (batch row,
-// channel), lane l holding states l, l+32, ... in registers, with no shared
-// memory staging.  The chunked kernel above stages and steps through a whole
-// 16-32-step chunk and pays its per-CTA set-up for every 8-16 channels, which
-// for one step costs ~40x the step itself; this kernel is bounded by reading
-// and writing the state.  Same arithmetic as the chunked kernel (A rounded
-// like the reference's op, the HiPPO form h' = h + e (h + w) when log_A has the
-// HiPPO structure -- tested per channel here, per CTA there -- and the general
-// (A_bar - 1)/A form otherwise), but each state's exponential is taken
-// directly instead of by the chunked kernel's product chain, and C.h is summed
-// by a warp reduction: results agree with it to a few float32 ulps.
+// Short sequences (decode steps, T <= kStepMaxT).  The chunked kernel stages
+// and steps through a whole 32-step chunk and pays its per-CTA set-up for a
+// few channels, which for one step costs many times the step itself; this
+// kernel is bounded by reading and writing the state.  A 256-thread CTA owns
+// CPS = 256/TPC channels of one batch row; thread (channel, sub) keeps states
+// [8 sub, 8 sub + 8) in registers, exactly the slice a thread of the chunked
+// kernel holds with 8 states per thread, and B/(n+1) and C of the step are
+// read once per CTA into shared memory.  The arithmetic is the chunked
+// kernel's, operation for operation (per-channel HiPPO decision, the same
+// records and decay chain, the same C.h summation tree), so a sequence
+// stepped through this kernel reproduces the chunked kernel's 8-state-per-
+// thread results bit for bit.
 constexpr int kStepMaxT = 4;
-constexpr int kStepWarps = 8;
+constexpr int kStepThreads = 256;
 
-template <int DT, int SDT, int NPT>
-__global__ void __launch_bounds__(32 * kStepWarps)
+template <int DT, int SDT, int TPC>
+__global__ void __launch_bounds__(kStepThreads)
 ssm_step_kernel(ScanArgs a) {
     using E = Elem<DT>;
     using T = typename E::T;
-    const int lane = threadIdx.x & 31;
-    const int64_t c = (int64_t)blockIdx.x * kStepWarps + (threadIdx.x >> 5), b = blockIdx.y;
+    constexpr int NPT = 8, NPR = 4, NP = TPC * NPT, CPS = kStepThreads / TPC;
+    __shared__ __align__(16) float s_B[NP];
+    __shared__ __align__(16) float s_C[NP];
+    const int tid = threadIdx.x, cl = tid / TPC, sub = tid % TPC, lane = tid & 31;
+    const unsigned gmask = TPC >= 32 ? 0xffffffffu : (((1u << TPC) - 1u) << (lane & ~(TPC - 1)));
+    const int64_t c = (int64_t)blockIdx.x * CPS + cl, b = blockIdx.y;
     const int64_t d = a.d, N = a.N, Tl = a.T;
-    if (c >= d) return;                                   // whole warps leave together
+    const bool live = c < d;
     const int64_t ld_bc = a.ld_bc > 0 ? a.ld_bc : N;
-    const T* logA = static_cast<const T*>(a.log_A) + c * N;
-    const float la0 = E::load(logA);
-    const float Abase = -E::rnd(expf(la0));
-    float A2[NPT], ci[NPT], limf[NPT], h[NPT];
+    const T* logA = static_cast<const T*>(a.log_A) + (live ? c : 0) * N;
+    const float la0 = live ? E::load(logA) : 0.f;
+    const float Abase = live ? -E::rnd(expf(la0)) : -1.f;
+    float2 hv[NPR], A2v[NPR], civ[NPR], lmv[NPR];
     bool ok = true;
 #pragma unroll
     for (int j = 0; j < NPT; ++j) {
-        const int64_t n = lane + 32 * j;
-        const bool on = n < N;
-        const float la = on ? E::load(logA + n) : 0.f;
-        const float A = on ? -E::rnd(expf(la)) : 0.f;
-        h[j] = 0.f;
-        if (on && a.state_in) {
-            const int64_t si = (b * d + c) * N + n;
-            h[j] = SDT == NT_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.state_in)[si])
-                                  : static_cast<const float*>(a.state_in)[si];
-        }
+        const int64_t n = (int64_t)sub * NPT + j;
+        const bool on = live && n < N;
+        float A = 0.f, h0 = 0.f;
         if (on) {
+            const float la = E::load(logA + n);
+            A = -E::rnd(expf(la));
+            if (a.state_in) {
+                const int64_t si = (b * d + c) * N + n;
+                h0 = SDT == NT_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.state_in)[si])
+                                    : static_cast<const float*>(a.state_in)[si];
+            }
             if (DT == NT_BF16) {
                 int e2;
                 frexpf(la, &e2);
@@ -642,13 +701,18 @@ ssm_step_kernel(ScanArgs a) {
         }
         const bool lim = on && fabsf(A) < 1e-6f;
         if (lim) ok = false;
-        limf[j] = lim ? 1.f : 0.f;
-        A2[j] = A * kLog2e;
-        ci[j] = (lim || A == 0.f) ? 0.f : 1.0f / A;
+        const float np1 = (float)(n + 1);
+        const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
+        float* hp = (j & 1) ? &hv[j / 2].y : &hv[j / 2].x;
+        *hp = h0;
+        if (j & 1) { A2v[j / 2].y = A * kLog2e; civ[j / 2].y = ci; lmv[j / 2].y = lim ? np1 : 0.f; }
+        else { A2v[j / 2].x = A * kLog2e; civ[j / 2].x = ci; lmv[j / 2].x = lim ? np1 : 0.f; }
     }
-    const bool hippo = __all_sync(0xffffffffu, ok);
-    const float rA0 = 1.0f / Abase;
-    const float Dv = E::load(static_cast<const T*>(a.D) + c);
+    const unsigned okm = __ballot_sync(0xffffffffu, ok);
+    const bool hippo = (okm & gmask) == gmask;
+    const float a0l = Abase * kLog2e, ra0 = 1.0f / Abase;
+    const float np1a = (float)(sub * NPT + 1), np1b = (float)(sub * NPT + 2);
+    const float Dv = live ? E::load(static_cast<const T*>(a.D) + c) : 0.f;
     const bool sparse_rows = a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
     const T* p_u = static_cast<const T*>(a.u);
     const T* p_dt = static_cast<const T*>(a.dt);
@@ -657,29 +721,49 @@ ssm_step_kernel(ScanArgs a) {
     const T* p_g = static_cast<const T*>(a.gate);
     for (int64_t t = 0; t < Tl; ++t) {
         const int64_t row = b * Tl + t;
-        const float u = E::to_f(p_u[row * d + c]);
-        const float dtv = E::to_f(p_dt[row * d + c]);
-        float y = 0.f;
-#pragma unroll
-        for (int j = 0; j < NPT; ++j) {
-            const int64_t n = lane + 32 * j;
-            if (n >= N) continue;
-            const float Bn = E::to_f(p_B[row * ld_bc + n]);
-            const float Cn = E::to_f(p_C[row * ld_bc + n]);
-            if (hippo) {
-                const float e = ex2(dtv * ((float)(n + 1) * Abase * kLog2e)) - 1.0f;
-                const float tv = __fmaf_rn(Bn * (1.0f / (float)(n + 1)), u * rA0, h[j]);
-                h[j] = __fmaf_rn(e, tv, h[j]);
-            } else {
-                const float av = ex2(dtv * A2[j]);
-                const float coef = __fmaf_rn(dtv, limf[j], __fmaf_rn(av, ci[j], -ci[j]));
-                h[j] = __fmaf_rn(av, h[j], coef * (Bn * u));
-            }
-            y = __fmaf_rn(Cn, h[j], y);
+        __syncthreads();                                    // the previous step's B/C reads are done
+        for (int i = tid; i < NP; i += kStepThreads) {
+            const bool in = i < N;
+            s_B[i] = in ? E::to_f(p_B[row * ld_bc + i]) * (1.0f / (float)(i + 1)) : 0.f;
+            s_C[i] = in ? E::to_f(p_C[row * ld_bc + i]) : 0.f;
         }
+        __syncthreads();
+        const float u = live ? E::to_f(p_u[row * d + c]) : 0.f;
+        const float dtv = live ? E::to_f(p_dt[row * d + c]) : 0.f;
+        float2 Bp[NPR], Cp[NPR], av[NPR];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
-        if (lane == 0) {
+        for (int j = 0; j < NPR; ++j) {
+            Bp[j] = *reinterpret_cast<const float2*>(s_B + sub * NPT + 2 * j);
+            Cp[j] = *reinterpret_cast<const float2*>(s_C + sub * NPT + 2 * j);
+        }
+        if (hippo) {
+            // the chunked kernel's record and chain (put_rec, step)
+            const float x0 = dtv * a0l, s = u * ra0;
+            const float q = ex2(x0);
+            const float qs = q * q, qm = __fmaf_rn(q, q, -1.0f);
+            av[0] = make_float2(ex2(x0 * np1a) - 1.0f, ex2(x0 * np1b) - 1.0f);
+            const float2 qq = make_float2(qs, qs), qqm = make_float2(qm, qm), ss = make_float2(s, s);
+#pragma unroll
+            for (int j = 1; j < NPR; ++j) av[j] = pfma(av[j - 1], qq, qqm);
+#pragma unroll
+            for (int j = 0; j < NPR; ++j) hv[j] = pfma(av[j], pfma(Bp[j], ss, hv[j]), hv[j]);
+        } else {
+            const float2 uu = make_float2(u, u), dd = make_float2(dtv, dtv);
+#pragma unroll
+            for (int j = 0; j < NPR; ++j) {
+                av[j] = make_float2(ex2(dtv * A2v[j].x), ex2(dtv * A2v[j].y));
+                const float2 coef = pfma(dd, lmv[j], pfma(av[j], civ[j], make_float2(-civ[j].x, -civ[j].y)));
+                const float2 bu = pmul(coef, pmul(Bp[j], uu));
+                hv[j] = pfma(av[j], hv[j], bu);
+            }
+        }
+        float2 ya = pmul(Cp[0], hv[0]), yb = pmul(Cp[1], hv[1]);
+        ya = pfma(Cp[2], hv[2], ya);
+        yb = pfma(Cp[3], hv[3], yb);
+        float y = (ya.x + yb.x) + (ya.y + yb.y);
+#pragma unroll
+        for (int half = TPC / 2; half >= 1; half >>= 1) y += __shfl_xor_sync(gmask, y, half);
+        if (sub == 0 && live) {
             const float yv = __fadd_rn(y, __fmul_rn(Dv, u));
             float o = E::rnd(yv);
             if (p_g) {
@@ -691,27 +775,34 @@ ssm_step_kernel(ScanArgs a) {
             if (orow >= 0) static_cast<T*>(a.y)[orow * d + c] = E::from_f(o);
         }
     }
-    if (a.state_out) {
+    if (a.state_out && live) {
 #pragma unroll
         for (int j = 0; j < NPT; ++j) {
-            const int64_t n = lane + 32 * j;
+            const int64_t n = (int64_t)sub * NPT + j;
             if (n >= N) continue;
             const int64_t si = (b * d + c) * N + n;
-            if (SDT == NT_BF16) static_cast<__nv_bfloat16*>(a.state_out)[si] = __float2bfloat16_rn(h[j]);
-            else static_cast<float*>(a.state_out)[si] = h[j];
+            const float hj = (j & 1) ? hv[j / 2].y : hv[j / 2].x;
+            if (SDT == NT_BF16) static_cast<__nv_bfloat16*>(a.state_out)[si] = __float2bfloat16_rn(hj);
+            else static_cast<float*>(a.state_out)[si] = hj;
         }
     }
 }
 
 template <int DT, int SDT>
 int launch_step(const ScanArgs& a, cudaStream_t stream) {
-    dim3 grid((unsigned)((a.d + kStepWarps - 1) / kStepWarps), (unsigned)a.B);
-    const int npt = a.N <= 32 ? 1 : a.N <= 64 ? 2 : a.N <= 128 ? 4 : 8;
-    switch (npt) {
-        case 1: ssm_step_kernel<DT, SDT, 1><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
-        case 2: ssm_step_kernel<DT, SDT, 2><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
-        case 4: ssm_step_kernel<DT, SDT, 4><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
-        default: ssm_step_kernel<DT, SDT, 8><<<grid, 32 * kStepWarps, 0, stream>>>(a); break;
+    const int tpc = pow2_at_least((a.N + 7) / 8);
+    auto go = [&](auto kern, int tpc_) {
+        dim3 grid((unsigned)((a.d + kStepThreads / tpc_ - 1) / (kStepThreads / tpc_)), (unsigned)a.B);
+        kern<<<grid, kStepThreads, 0, stream>>>(a);
+    };
+    switch (tpc) {
+        case 1: go(ssm_step_kernel<DT, SDT, 1>, 1); break;
+        case 2: go(ssm_step_kernel<DT, SDT, 2>, 2); break;
+        case 4: go(ssm_step_kernel<DT, SDT, 4>, 4); break;
+        case 8: go(ssm_step_kernel<DT, SDT, 8>, 8); break;
+        case 16: go(ssm_step_kernel<DT, SDT, 16>, 16); break;
+        case 32: go(ssm_step_kernel<DT, SDT, 32>, 32); break;
+        default: return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)a.N);
     }
     return check_launch("ssm_step_kernel");
 }

@@ -55,6 +55,9 @@ _SIGS = {
     "nt_block_forward": ([_I32, _I32, _I64, _I64, _I64, _I64, _I64] + [_P] * 17 + [_I32, _P, _I64, _P], _I32),
     "nt_lif_ssm_fused": ([_I64, _I64, _I64, _I64] + [_P] * 14 + [_I32, _P, _P], _I32),
     "nt_window_attention": ([_I32, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _I64, _P], _I32),
+    "nt_embedding": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P], _I32),
+    "nt_lm_head_workspace_bytes": ([_I32, _I64, _I64, _I64], _I64),
+    "nt_lm_head": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P], _I32),
 }
 
 EXPORTED = tuple(_SIGS)
@@ -357,6 +360,36 @@ def window_attention(qkv: Tensor, n_heads: int, window: int, cos: Tensor, sin: T
                                     _p(cos), _p(sin), _p(out), out.stride(1), _stream(dev))
     _check("nt_window_attention", rc)
     return out
+
+
+def embedding(ids: Tensor, W: Tensor) -> Tensor:
+    """nn.Embedding lookup (model.py:258): ids [...] int64 -> [..., d_model] in W's dtype.
+    An id outside [0, vocab) gives a zero row and a flag in the device error word."""
+    dev = _require_cuda(ids, W)
+    W = _c(W)
+    ids = ids.to(torch.int64).contiguous()
+    vocab, dm = W.shape
+    out = torch.empty((*ids.shape, dm), dtype=W.dtype, device=dev)
+    rc = load().nt_embedding(_dtype_code(W), ids.numel(), dm, vocab, _p(ids), _p(W), _p(out), _stream(dev))
+    _check("nt_embedding", rc)
+    return out
+
+
+def lm_head(x: Tensor, gamma: Tensor, W: Tensor, workspace: Optional[Tensor] = None) -> Tensor:
+    """Final RMSNorm + tied lm_head (model.py:283-284): x [..., dm] -> logits [..., vocab] in x.dtype."""
+    dev = _require_cuda(x, gamma, W)
+    a = x.dtype
+    dm = x.shape[-1]
+    vocab = W.shape[0]
+    M = x.numel() // dm
+    x2, g2, W2 = _c(x), _c(gamma, a), _c(W, a)
+    logits = torch.empty((*x.shape[:-1], vocab), dtype=a, device=dev)
+    L = load()
+    nbytes = L.nt_lm_head_workspace_bytes(_DT[a], M, dm, vocab)
+    ws = workspace if (workspace is not None and workspace.numel() >= nbytes) else _workspace(nbytes, dev)
+    rc = L.nt_lm_head(_DT[a], M, dm, vocab, _p(x2), _p(g2), _p(W2), _p(logits), _p(ws), ws.numel(), _stream(dev))
+    _check("nt_lm_head", rc)
+    return logits
 
 
 def launch_count() -> int:

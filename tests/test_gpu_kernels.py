@@ -52,7 +52,8 @@ def test_lif_golden_bit_exact(nat, mode):
 
 
 @pytest.mark.parametrize("mode", ["fp32", "bf16"])
-@pytest.mark.parametrize("shape", [(1, 1, 1), (2, 65, 129), (3, 300, 333), (1, 2048, 1280)])
+@pytest.mark.parametrize("shape", [(1, 1, 1), (2, 65, 129), (3, 300, 333), (1, 2048, 1280), (64, 1, 4096),
+                                   (5, 17, 200), (2, 32, 129)])
 def test_lif_random_bit_exact(nat, mode, shape):
     rng = np.random.default_rng(7)
     B, Tn, C = shape
@@ -515,6 +516,53 @@ def test_selective_scan_mixed_hippo_channels(nat):
         ys.append(yk)
     np.testing.assert_allclose(N(torch.cat(ys, 1)), N(y), rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(N(s_k), N(s), rtol=1e-4, atol=1e-6)
+
+
+# --------------------------------------------------------------------------- #
+#  Model glue: embedding gather, final RMSNorm + tied lm_head (model.py:258,283-284)
+# --------------------------------------------------------------------------- #
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_embedding_gather_exact(nat, dtype):
+    g = torch.Generator(device=DEV).manual_seed(3)
+    W = torch.randn(1000, 96, device=DEV, generator=g).to(dtype)
+    ids = torch.randint(0, 1000, (3, 77), device=DEV, generator=g)
+    assert torch.equal(nat.embedding(ids, W), W[ids])
+    W2 = torch.randn(50, 13, device=DEV, generator=g).to(dtype)            # rows not 16-byte multiples
+    ids2 = torch.randint(0, 50, (1, 9), device=DEV, generator=g)
+    assert torch.equal(nat.embedding(ids2, W2), W2[ids2])
+
+
+def test_embedding_bad_id_flags_and_zeroes(nat):
+    """An id outside [0, vocab) gives a zero row and the bad-argument flag in the
+    device error word (the reference raises IndexError; the kernel cannot)."""
+    W = torch.randn(10, 64, device=DEV)
+    nat.device_error_flags(0)                               # start from a clear word
+    ids = torch.tensor([[1, 10, -1, 3]], device=DEV)
+    out = nat.embedding(ids, W)
+    assert torch.equal(out[0, 0], W[1]) and torch.equal(out[0, 3], W[3])
+    assert torch.count_nonzero(out[0, 1:3]).item() == 0
+    assert nat.device_error_flags(0) == 8                   # ERRF_BAD_ARG, then cleared
+    assert nat.device_error_flags(0) == 0
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("M,dm,vocab", [(64, 96, 32000), (300, 640, 1000), (5, 2048, 4100)])
+def test_lm_head_vs_oracle(nat, mode, M, dm, vocab):
+    rng = np.random.default_rng(M + dm)
+    x = rng.normal(0, 1, (M, dm)).astype(np.float32)
+    gam = rng.uniform(0.5, 1.5, dm).astype(np.float32)
+    W = rng.normal(0, 0.02, (vocab, dm)).astype(np.float32)
+    dt = torch.float32 if mode == "fp32" else torch.bfloat16
+    if mode == "bf16":
+        x, gam, W = O.bf16(x), O.bf16(gam), O.bf16(W)
+    logits = nat.lm_head(T(x, dt), T(gam, dt), T(W, dt))
+    ref = O._mm(O.rmsnorm(x, gam, mode), W, mode)
+    assert logits.dtype == dt and logits.shape == (M, vocab)
+    if mode == "fp32":
+        np.testing.assert_allclose(N(logits), ref, rtol=1e-4, atol=1e-5)
+    else:
+        np.testing.assert_allclose(N(logits), ref, rtol=2e-2, atol=2e-2)
 
 
 # --------------------------------------------------------------------------- #

@@ -59,9 +59,16 @@ def _check_block(blk, x, state=None, spike_floor=0.995):
     assert agree >= spike_floor, agree
     assert abs(int(count.item()) - rm["spike_count"]) <= 0.01 * rm["spike_count"] + 2
     np.testing.assert_allclose(N(out), ro, rtol=2e-2, atol=2e-2)
-    np.testing.assert_allclose(N(st.membrane), rst.membrane, rtol=2e-2, atol=2e-2)
-    scale = max(float(np.abs(rst.ssm_state).max()), 1e-6)
-    np.testing.assert_allclose(N(st.ssm_state), rst.ssm_state, rtol=2e-2, atol=2e-2 * scale)
+    # a spike flipped at the threshold leaves that channel's membrane ~theta apart:
+    # at most the flipped fraction may differ, the rest within tolerance
+    mem_bad = ~np.isclose(N(st.membrane), rst.membrane, rtol=2e-2, atol=2e-2)
+    assert mem_bad.mean() <= 1.0 - spike_floor, mem_bad.mean()
+    # the reference rounds its bf16 state (at random init dt ~ 1e-8 leaves it exactly 0,
+    # where the float32 state keeps ~1e-7): atol 2 % of the state's scale, at least 2e-4
+    # (a flipped spike also moves every state of its channel: the same allowance)
+    scale = max(float(np.abs(rst.ssm_state).max()), 1e-2)
+    st_bad = ~np.isclose(N(st.ssm_state), rst.ssm_state, rtol=2e-2, atol=2e-2 * scale)
+    assert st_bad.mean() <= 1.0 - spike_floor, st_bad.mean()
     return BlockState(membrane=st.membrane, ssm_state=st.ssm_state), agree
 
 

@@ -26,6 +26,7 @@
  *   nt_rmsnorm_in_proj     FusedSpikeBlock.norm + in_proj    neuratensor/core/fused.py:118-119
  *   nt_block_forward       FusedSpikeBlock.forward     neuratensor/core/fused.py:101-147
  *   nt_window_attention    SlidingWindowAttention RoPE + SDPA neuratensor/core/model.py:148-178
+ *   nt_attention_forward   SlidingWindowAttention.forward neuratensor/core/model.py:148-181
  *   nt_embedding           NeuraTensorModel.embedding  neuratensor/core/model.py:258
  *   nt_lm_head             NeuraTensorModel.norm + lm_head neuratensor/core/model.py:283-284
  *   nt_lif_ssm_fused       LIF spikes driving the selective scan with given dt/B/C
@@ -79,6 +80,13 @@ NT_API int nt_device_supported(int device);
  * a bounded wait expires.  Synchronises the device.  *flags == 0 means no
  * kernel reported an error. */
 NT_API int nt_get_error_flag(int device, unsigned* flags, int clear);
+/* Checks the bounded-wait path (no counterpart in the reference, whose code
+ * never waits on the device): one CTA waits on a barrier that nothing
+ * completes, gives up after limit_ns of wall time (0..1e9), sets bit 16 of the
+ * device error word and returns normally.  Every pipeline wait in this
+ * library's kernels is bounded the same way (2 s), so a stalled producer shows
+ * up as a flag and an error status instead of a hung GPU. */
+NT_API int nt_bounded_wait_check(int64_t limit_ns, void* stream);
 /* Kernels this library has launched in this process (all devices, all host
  * threads).  Reading it before and after a call counts that call's launches.
  * No counterpart in the reference, which launches no kernels of its own. */
@@ -162,6 +170,17 @@ NT_API size_t nt_noalloc_scratch_bytes(void);
 NT_API int nt_rmsnorm_in_proj_noalloc(int dtype, int64_t M, int64_t dm, int64_t di,
                        const void* x, const void* gamma, const void* W_in,
                        void* h, void* gate, void* stream);
+
+/* SlidingWindowAttention.forward (model.py:148-181), bf16, head_dim 64 or 128:
+ * out = o_proj(attention(qkv(RMSNorm(x)))) + x, with the attention as in
+ * nt_window_attention.  x, out: [B,T,dm]; norm_w: [dm]; W_qkv: [3*dm, dm];
+ * W_o: [dm, dm]; cos_t, sin_t: [T, dm/n_heads] rotary tables.
+ * Workspace: nt_attention_workspace_bytes(). */
+NT_API int64_t nt_attention_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t dm);
+NT_API int nt_attention_forward(int dtype, int64_t B, int64_t T, int64_t dm, int64_t n_heads, int64_t window,
+                                const void* x, const void* norm_w, const void* W_qkv, const void* W_o,
+                                const void* cos_t, const void* sin_t, void* out,
+                                void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Embedding gather -- NeuraTensorModel.embedding (model.py:258, nn.Embedding):
  * out[r, :] = W[ids[r], :] for r < M.  ids: [M] int64; W: [vocab, dm]; out:

@@ -8,9 +8,9 @@ initialisation order (embedding, blocks with attention interleaved, final
 norm, tied lm_head, then ``_init_weights``), so a seed gives the reference's
 weights and checkpoints load either way.
 
-The spike blocks, the embedding gather, the sliding-window attention core
-and the final RMSNorm + tied lm_head (bf16 logits on the tcgen05 GEMM) run on
-the native kernels; the attention's RMSNorm and projections are torch ops.
+The spike blocks, the embedding gather, the sliding-window attention layers
+(RMSNorm, projections and the windowed attention core) and the final RMSNorm +
+tied lm_head (bf16 logits on the tcgen05 GEMM) run on the native kernels.
 The forward collects every block's spike count in one device buffer and
 reads it once, instead of the reference's three host syncs per block.
 """
@@ -128,15 +128,14 @@ class SlidingWindowAttention(nn.Module):
             return self.forward_native(x)
         return self.forward_torch(x)
 
-    def forward_native(self, x: Tensor) -> Tensor:
-        """RMSNorm and the projections as torch ops; RoPE, the windowed causal
-        softmax attention and the head merge in one kernel (nt_window_attention)."""
+    def forward_native(self, x: Tensor, workspace: Optional[Tensor] = None) -> Tensor:
+        """The whole layer in one native call (nt_attention_forward): RMSNorm, the
+        qkv projection and o_proj + residual on the tcgen05 GEMM, RoPE and the
+        windowed causal softmax attention in one kernel."""
         from .. import native
-        B, T, _ = x.shape
-        qkv = self.qkv(self.norm(x))
-        cos, sin = self.rope(qkv)                   # rows [0, T): qkv.shape[-2] == T
-        o = native.window_attention(qkv, self.n_heads, self.window, cos, sin)
-        return self.o_proj(o) + x
+        cos, sin = self.rope(x)                     # rows [0, T) in x's dtype
+        return native.attention_forward(x, self.norm.weight, self.qkv.weight, self.o_proj.weight, self.n_heads,
+                                        self.window, cos, sin, workspace=workspace)
 
     def forward_torch(self, x: Tensor) -> Tensor:
         """The reference's op sequence (fp32, CPU tensors, head dims other than 64 and 128)."""

@@ -187,6 +187,42 @@ int nt_get_error_flag(int device, unsigned* flags, int clear) {
 }
 
 // ---------------------------------------------------------------------------
+// Bounded-wait check: one CTA waits on a shared-memory mbarrier that nothing
+// ever completes, with a caller-chosen wall-time limit (at most 1 s), the way
+// the GEMM's pipeline waits are bounded.  When the limit passes, the kernel
+// sets the wait-expired bit of the device error word and returns normally, so
+// the context stays usable; nt_get_error_flag then reports the bit.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr unsigned ERRF_WAIT_CHECK = 16u;
+
+__global__ void bounded_wait_check_kernel(uint64_t limit_ns, unsigned* err) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);                     // one arrival expected, none ever made
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    const uint64_t t0 = globaltimer_ns();
+    bool done = false;
+    while (!done && globaltimer_ns() - t0 < limit_ns) done = mbar_try_wait(smem_u32(&bar), 0);
+    if (!done) atomicOr(err, ERRF_WAIT_CHECK);
+}
+}  // namespace
+
+int nt_bounded_wait_check(int64_t limit_ns, void* stream) {
+    if (limit_ns < 0 || limit_ns > 1000000000LL)
+        return fail(NT_ERR_ARG, "nt_bounded_wait_check: limit %lld ns outside [0, 1 s]", (long long)limit_ns);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    unsigned* w = device_error_word(dev);
+    if (!w) return fail(NT_ERR_CUDA, "nt_bounded_wait_check: error word unavailable");
+    bounded_wait_check_kernel<<<1, 32, 0, as_stream(stream)>>>((uint64_t)limit_ns, w);
+    return check_launch("bounded_wait_check_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // (a) LIF
 // ---------------------------------------------------------------------------
 int nt_lif_scan(int dtype, int64_t B, int64_t T, int64_t C, const void* x, int64_t x_sb, int64_t x_st,
@@ -446,6 +482,52 @@ int nt_window_attention(int dtype, int64_t B, int64_t T, int64_t n_heads, int64_
         return fail(NT_ERR_ARG, "nt_window_attention: qkv/cos/sin need 16-byte aligned rows, out 4-byte");
     return launch_window_attention(B, T, n_heads, head_dim, window, qkv, ld_qkv, cos_t, sin_t, out, ld_out,
                                    as_stream(stream));
+}
+
+int64_t nt_attention_workspace_bytes(int dtype, int64_t B, int64_t T, int64_t dm) {
+    const int64_t M = B * T, es = esize(dtype);
+    return align256(M * dm * es) + align256(M * 3 * dm * es) + align256(M * dm * es);
+}
+
+int nt_attention_forward(int dtype, int64_t B, int64_t T, int64_t dm, int64_t n_heads, int64_t window,
+                         const void* x, const void* norm_w, const void* W_qkv, const void* W_o, const void* cos_t,
+                         const void* sin_t, void* out, void* workspace, int64_t workspace_bytes, void* stream) {
+    if (dtype != NT_BF16) return fail(NT_ERR_DTYPE, "nt_attention_forward: bf16 only (dtype %d)", dtype);
+    if (B < 1 || T < 1 || dm < 1 || n_heads < 1 || dm % n_heads)
+        return fail(NT_ERR_ARG, "nt_attention_forward: bad sizes");
+    const int64_t hd = dm / n_heads;
+    if (hd != 64 && hd != 128) return fail(NT_ERR_ARG, "nt_attention_forward: head_dim %lld (64 or 128)", (long long)hd);
+    if (!x || !norm_w || !W_qkv || !W_o || !cos_t || !sin_t || !out)
+        return fail(NT_ERR_ARG, "nt_attention_forward: null pointer");
+    const int64_t need = nt_attention_workspace_bytes(dtype, B, T, dm);
+    if (!workspace || workspace_bytes < need)
+        return fail(NT_ERR_WORKSPACE, "nt_attention_forward: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                    (long long)need);
+    NT_TRY(check_gemm_operand(W_qkv, dm, dtype, "nt_attention_forward(W_qkv)"));
+    NT_TRY(check_gemm_operand(W_o, dm, dtype, "nt_attention_forward(W_o)"));
+    const int64_t M = B * T, es = esize(dtype);
+    Carve c(workspace);
+    void* xn = c.take<char>(M * dm * es);
+    void* qkv = c.take<char>(M * 3 * dm * es);
+    void* o = c.take<char>(M * dm * es);
+    cudaStream_t st = as_stream(stream);
+    // norm -> qkv projection (model.py:156-158)
+    NT_TRY(launch_rmsnorm(dtype, M, dm, x, norm_w, xn, st));
+    {
+        GemmArgs g{};
+        g.M = M; g.N = 3 * dm; g.K = dm;
+        g.A = xn; g.lda = dm; g.Bw = W_qkv; g.ldb = dm;
+        g.epi.kind = EPI_STORE; g.epi.out = qkv; g.epi.ldo = 3 * dm;
+        NT_TRY(launch_gemm(dtype, g, st));
+    }
+    // RoPE + windowed causal softmax attention (model.py:159-179)
+    NT_TRY(nt_window_attention(dtype, B, T, n_heads, hd, window, qkv, 3 * dm, cos_t, sin_t, o, dm, stream));
+    // o_proj + residual (model.py:180-181)
+    GemmArgs g{};
+    g.M = M; g.N = dm; g.K = dm;
+    g.A = o; g.lda = dm; g.Bw = W_o; g.ldb = dm;
+    g.epi.kind = EPI_RESID; g.epi.out = out; g.epi.ldo = dm; g.epi.resid = x; g.epi.ldr = dm;
+    return launch_gemm(dtype, g, st);
 }
 
 int nt_lif_ssm_fused(int64_t B, int64_t L, int64_t d, int64_t N, const void* x, const void* delta, const void* Bm,

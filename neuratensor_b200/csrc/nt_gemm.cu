@@ -75,6 +75,10 @@ __device__ __forceinline__ void epi_apply(const EpiArgs& e, int64_t row, int64_t
         v = E::rnd(v * s);
         v = E::rnd(v + E::load(static_cast<const T*>(e.resid) + r * e.ldr + col));
         static_cast<T*>(e.out)[r * e.ldo + col] = E::from_f(v);
+    } else if (KIND == EPI_RESID) {
+        // o_proj(o) + x  (model.py:181): the product rounded, then the sum
+        const float v = E::rnd(E::rnd(acc) + E::load(static_cast<const T*>(e.resid) + row * e.ldr + col));
+        static_cast<T*>(e.out)[row * e.ldo + col] = E::from_f(v);
     } else {  // EPI_SCATTER
         const int64_t r = out_row(e, row);
         static_cast<T*>(e.out)[r * e.ldo + col] = E::from_f(acc);
@@ -118,7 +122,7 @@ __device__ __forceinline__ uint4 epi_pre8(const EpiArgs& e, int64_t orow, int64_
     if (!epi_vec8(e, col, N)) return make_uint4(0, 0, 0, 0);
     if (KIND == EPI_SSM_PROJ && col < e.split)
         return __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.bias) + col));
-    if (KIND == EPI_OUT_PROJ)
+    if (KIND == EPI_OUT_PROJ || KIND == EPI_RESID)
         return __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(e.resid) + orow * e.ldr + col));
     return make_uint4(0, 0, 0, 0);
 }
@@ -173,6 +177,12 @@ __device__ __forceinline__ void epi_fin8(const EpiArgs& e, int64_t row, int64_t 
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = E::rnd(E::rnd(E::rnd(acc[j]) * s) + res[j]);
         dst = static_cast<__nv_bfloat16*>(e.out) + orow * e.ldo + col;
+    } else if (KIND == EPI_RESID) {
+        float res[8];
+        unpack_bf16x8(pre, res);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = E::rnd(E::rnd(acc[j]) + res[j]);
+        dst = static_cast<__nv_bfloat16*>(e.out) + row * e.ldo + col;
     } else {  // EPI_SCATTER
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = acc[j];
@@ -579,7 +589,7 @@ int launch_gemm(int dtype, const GemmArgs& g_in, cudaStream_t stream) {
         if (e.kind == EPI_SPLIT2 || e.kind == EPI_SSM_PROJ || e.kind == EPI_SPLIT2_SILU)
             v = v && e.split % 8 == 0 && al16(e.out2) && e.ldo2 % 8 == 0;
         if (e.kind == EPI_SSM_PROJ) v = v && al16(e.bias);
-        if (e.kind == EPI_OUT_PROJ) v = v && al16(e.resid) && e.ldr % 8 == 0;
+        if (e.kind == EPI_OUT_PROJ || e.kind == EPI_RESID) v = v && al16(e.resid) && e.ldr % 8 == 0;
         g.epi.vec = v ? 1 : 0;
     }
     switch (g.epi.kind) {
@@ -588,6 +598,7 @@ int launch_gemm(int dtype, const GemmArgs& g_in, cudaStream_t stream) {
         case EPI_SSM_PROJ: return launch_kind<EPI_SSM_PROJ>(dtype, g, stream);
         case EPI_OUT_PROJ: return launch_kind<EPI_OUT_PROJ>(dtype, g, stream);
         case EPI_SCATTER: return launch_kind<EPI_SCATTER>(dtype, g, stream);
+        case EPI_RESID: return launch_kind<EPI_RESID>(dtype, g, stream);
         case EPI_SPLIT2_SILU: return launch_kind<EPI_SPLIT2_SILU>(dtype, g, stream);
         default: return fail(NT_ERR_ARG, "gemm: epilogue kind %d", g.epi.kind);
     }

@@ -86,7 +86,7 @@ int launch_gather_rows(int dtype, int64_t M, int64_t K, const void* src, const i
 int launch_fill_inactive(int dtype, int64_t M, int64_t N, const int* row_pos, const int* counters,
                          const void* src, void* dst, cudaStream_t stream);
 
-// Sliding-window causal attention with RoPE, bf16, head_dim 64: qkv row-major
+// Sliding-window causal attention with RoPE, bf16, head_dim 64 or 128: qkv row-major
 // [B*T, ld_qkv] with columns [q | k | v] (H heads of 64 each), cos/sin [T][64]
 // bf16, out [B*T, ld_out] (head h in columns h*64 .. h*64+63).
 int launch_window_attention(int64_t B, int64_t T, int64_t H, int64_t head_dim, int64_t window, const void* qkv,
@@ -102,7 +102,8 @@ enum EpiKind : int {
     EPI_SSM_PROJ = 2,     // cols [0,split): softplus(acc + bias) -> out (dt); rest -> out2 (B|C)
     EPI_OUT_PROJ = 3,     // out[row_map(r)] = rnd(rnd(rnd(acc)*scale) + resid[row_map(r)])
     EPI_SCATTER = 4,      // out[row_map(r)] = acc  (sparse out_proj without scale)
-    EPI_SPLIT2_SILU = 5   // cols [0,split) -> out (h), [split,N) -> out2 as rnd(silu(acc))
+    EPI_SPLIT2_SILU = 5,  // cols [0,split) -> out (h), [split,N) -> out2 as rnd(silu(acc))
+    EPI_RESID = 6         // out = rnd(rnd(acc) + resid)  (attention o_proj + residual)
 };
 struct EpiArgs {
     int kind;

@@ -41,6 +41,7 @@ _SIGS = {
     "nt_device_supported": ([_I32], _I32),
     "nt_get_error_flag": ([_I32, ctypes.POINTER(ctypes.c_uint), _I32], _I32),
     "nt_launch_count": ([], ctypes.c_ulonglong),
+    "nt_bounded_wait_check": ([_I64, _P], _I32),
     "nt_lif_scan": ([_I32, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P], _I32),
     "nt_selective_scan": ([_I32, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I32),
     "nt_ssm_workspace_bytes": ([_I32, _I64, _I64, _I64, _I64], _I64),
@@ -56,6 +57,8 @@ _SIGS = {
     "nt_lif_ssm_fused": ([_I64, _I64, _I64, _I64] + [_P] * 14 + [_I32, _P, _P], _I32),
     "nt_window_attention": ([_I32, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _I64, _P], _I32),
     "nt_embedding": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P], _I32),
+    "nt_attention_workspace_bytes": ([_I32, _I64, _I64, _I64], _I64),
+    "nt_attention_forward": ([_I32, _I64, _I64, _I64, _I64, _I64] + [_P] * 8 + [_I64, _P], _I32),
     "nt_lm_head_workspace_bytes": ([_I32, _I64, _I64, _I64], _I64),
     "nt_lm_head": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P], _I32),
 }
@@ -362,6 +365,31 @@ def window_attention(qkv: Tensor, n_heads: int, window: int, cos: Tensor, sin: T
     return out
 
 
+def attention_forward(x: Tensor, norm_w: Tensor, W_qkv: Tensor, W_o: Tensor, n_heads: int, window: int,
+                      cos: Tensor, sin: Tensor, workspace: Optional[Tensor] = None) -> Tensor:
+    """SlidingWindowAttention.forward (model.py:148-181) in one call: RMSNorm, qkv
+    projection, RoPE + windowed causal attention, o_proj + residual.  bf16, head_dim 64 or 128."""
+    dev = _require_cuda(x, norm_w, W_qkv, W_o, cos, sin)
+    if x.dtype != torch.bfloat16:
+        raise NativeError("nt_attention_forward", 2, "bf16 only")
+    B, T, dm = x.shape
+    hd = dm // n_heads
+    x = x.contiguous()
+    nw, Wq, Wo = _c(norm_w, x.dtype), _c(W_qkv, x.dtype), _c(W_o, x.dtype)
+    cos = cos[:T].to(torch.bfloat16).contiguous()
+    sin = sin[:T].to(torch.bfloat16).contiguous()
+    if cos.shape != (T, hd) or sin.shape != (T, hd):
+        raise ValueError(f"cos/sin must hold at least T rows of {hd}")
+    out = torch.empty_like(x)
+    L = load()
+    nbytes = L.nt_attention_workspace_bytes(_DT[x.dtype], B, T, dm)
+    ws = workspace if (workspace is not None and workspace.numel() >= nbytes) else _workspace(nbytes, dev)
+    rc = L.nt_attention_forward(_DT[x.dtype], B, T, dm, n_heads, int(window), _p(x), _p(nw), _p(Wq), _p(Wo),
+                                _p(cos), _p(sin), _p(out), _p(ws), ws.numel(), _stream(dev))
+    _check("nt_attention_forward", rc)
+    return out
+
+
 def embedding(ids: Tensor, W: Tensor) -> Tensor:
     """nn.Embedding lookup (model.py:258): ids [...] int64 -> [..., d_model] in W's dtype.
     An id outside [0, vocab) gives a zero row and a flag in the device error word."""
@@ -395,6 +423,12 @@ def lm_head(x: Tensor, gamma: Tensor, W: Tensor, workspace: Optional[Tensor] = N
 def launch_count() -> int:
     """Kernels this library has launched in this process (nt_launch_count)."""
     return int(load().nt_launch_count())
+
+
+def bounded_wait_check(limit_ns: int, device: Optional[torch.device] = None) -> None:
+    """Launch the bounded-wait check on the current stream (nt_bounded_wait_check)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    _check("nt_bounded_wait_check", load().nt_bounded_wait_check(int(limit_ns), _stream(dev)))
 
 
 def device_error_flags(device: int = 0, clear: bool = True) -> int:

@@ -546,6 +546,27 @@ def test_embedding_bad_id_flags_and_zeroes(nat):
     assert nat.device_error_flags(0) == 0
 
 
+def test_bounded_wait_expires_into_the_error_word(nat):
+    """A wait that nothing completes gives up after its limit (20 ms here), sets
+    its bit in the device error word and returns: the status reaches the host
+    and the context keeps working (a kernel launched afterwards is correct)."""
+    nat.device_error_flags(0)                               # start from a clear word
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    nat.bounded_wait_check(20_000_000)
+    t1.record()
+    torch.cuda.synchronize()
+    assert 15.0 <= t0.elapsed_time(t1) < 1000.0
+    assert nat.device_error_flags(0) == 16                  # reported, then cleared
+    assert nat.device_error_flags(0) == 0
+    W = torch.randn(10, 64, device=DEV)
+    ids = torch.tensor([[3, 1]], device=DEV)
+    assert torch.equal(nat.embedding(ids, W), W[ids])
+    with pytest.raises(nat.NativeError):
+        nat.bounded_wait_check(2_000_000_000)               # beyond the 1 s cap: rejected on the host
+
+
 @pytest.mark.parametrize("mode", ["fp32", "bf16"])
 @pytest.mark.parametrize("M,dm,vocab", [(64, 96, 32000), (300, 640, 1000), (5, 2048, 4100)])
 def test_lm_head_vs_oracle(nat, mode, M, dm, vocab):

@@ -17,32 +17,71 @@ namespace nt {
 // RMSNorm: y = rnd(rnd(x * 1/sqrt(mean(x^2) + eps)) * w), eps = FLT_EPSILON.
 // torch computes rms_norm in float32 for bf16 inputs and rounds the
 // normalised value to the input dtype before the weight multiply.
-// One warp per row.
+// One warp per row, 16-byte vectors per lane when rows allow.
 // ---------------------------------------------------------------------------
 template <int DT>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(int64_t M, int64_t D, const void* xv, const void* wv, void* yv) {
     using E = Elem<DT>;
     using T = typename E::T;
+    constexpr int EPV = 16 / (int)sizeof(T);           // elements per 16-byte vector
     const T* x = static_cast<const T*>(xv);
     const T* w = static_cast<const T*>(wv);
     T* y = static_cast<T*>(yv);
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    // 16-byte vectors per lane when every row starts 16-byte aligned
+    const bool vec = (D % EPV == 0) &&
+                     ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+    auto widen = [](const T* p, float (&v)[EPV]) {
+        if constexpr (sizeof(T) == 2) {
+            const uint4 q = *reinterpret_cast<const uint4*>(p);
+            const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[2 * i] = __uint_as_float(qq[i] << 16);
+                v[2 * i + 1] = __uint_as_float(qq[i] & 0xffff0000u);
+            }
+        } else {
+            const float4 q = *reinterpret_cast<const float4*>(p);
+            v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+        }
+    };
     for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < M; r += warps) {
         const T* xr = x + r * D;
+        T* yr = y + r * D;
         float ss = 0.f;
-        for (int64_t i = lane; i < D; i += 32) {
-            const float v = E::load(xr + i);
-            ss = fmaf(v, v, ss);
+        if (vec) {
+            for (int64_t i = (int64_t)lane * EPV; i < D; i += 32 * EPV) {
+                float v[EPV];
+                widen(xr + i, v);
+#pragma unroll
+                for (int k = 0; k < EPV; ++k) ss = fmaf(v[k], v[k], ss);
+            }
+        } else {
+            for (int64_t i = lane; i < D; i += 32) {
+                const float v = E::load(xr + i);
+                ss = fmaf(v, v, ss);
+            }
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         const float mean = ss / (float)D;
         const float rs = 1.0f / sqrtf(mean + 1.1920928955078125e-07f);
-        T* yr = y + r * D;
-        for (int64_t i = lane; i < D; i += 32) {
-            const float v = E::rnd(E::load(xr + i) * rs);
-            yr[i] = E::from_f(v * E::load(w + i));
+        if (vec) {
+            for (int64_t i = (int64_t)lane * EPV; i < D; i += 32 * EPV) {
+                float v[EPV], g[EPV];
+                widen(xr + i, v);
+                widen(w + i, g);
+                T o[EPV];
+#pragma unroll
+                for (int k = 0; k < EPV; ++k) o[k] = E::from_f(E::rnd(v[k] * rs) * g[k]);
+                *reinterpret_cast<uint4*>(yr + i) = *reinterpret_cast<const uint4*>(o);
+            }
+        } else {
+            for (int64_t i = lane; i < D; i += 32) {
+                const float v = E::rnd(E::load(xr + i) * rs);
+                yr[i] = E::from_f(v * E::load(w + i));
+            }
         }
     }
 }

@@ -109,6 +109,68 @@ __device__ __forceinline__ float2 pmul(float2 a, float2 b) {
 #endif
 }
 
+// One unit in the last place of a bf16 value held in a float: 2^(exponent - 7)
+// (0 for zero and subnormals, which are then compared exactly).
+__device__ __forceinline__ float bf16_ulp(float v) {
+    const uint32_t e = __float_as_uint(v) & 0x7f800000u;
+    return e <= (7u << 23) ? 0.f : __uint_as_float(e - (7u << 23));
+}
+// Eight consecutive states at p (16-byte vectors when p is aligned).
+__device__ __forceinline__ void load_state8(const __nv_bfloat16* p, float (&h)[8]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            h[2 * i] = __uint_as_float(ww[i] << 16);
+            h[2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = __bfloat162float(p[i]);
+    }
+}
+__device__ __forceinline__ void load_state8(const float* p, float (&h)[8]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+        h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w; h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = p[i];
+    }
+}
+__device__ __forceinline__ void store_state8(__nv_bfloat16* p, const float (&h)[8]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 v = __floats2bfloat162_rn(h[2 * i], h[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) p[i] = __float2bfloat16_rn(h[i]);
+    }
+}
+__device__ __forceinline__ void store_state8(float* p, const float (&h)[8]) {
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        *reinterpret_cast<float4*>(p) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(p + 4) = make_float4(h[4], h[5], h[6], h[7]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) p[i] = h[i];
+    }
+}
+// HiPPO test of one state of a bf16 model: log_A[c,n] == log(n+1) + log_A[c,0]
+// to one bf16 ulp of the stored value (the HiPPO init up to storage rounding).
+__device__ __forceinline__ bool hippo_state_bf16(float la, float la0, float lnp1) {
+    return fabsf(la - (lnp1 + la0)) <= bf16_ulp(la);
+}
+// exp(la) < 2e-6 is impossible above this log_A, so |A| < 1e-6 (the
+// reference's dt*B branch, ssm.py:129-137) needs A itself only below it.
+constexpr float kLimLogA = -13.0f;
+
 // Shared-memory plan of one CTA: CPB = K*128/TPC channels of one batch row,
 // 128 threads, TPC threads per channel slice holding NPT states each (NP =
 // TPC*NPT >= d_state), K channels per thread.
@@ -125,7 +187,7 @@ struct ScanLayout {
     // general-path per-state constants [3][K][NPT/2][128] float2
     static constexpr int YO_BYTES = ((TCH * CPB * (int)sizeof(T)) + 15) & ~15;
     static constexpr size_t BYTES =
-        2 * (size_t)RAW_BYTES + YO_BYTES + 4 * TCH + 4 * CPB + 8 * 3 * K * (NPT / 2) * 128;
+        2 * (size_t)RAW_BYTES + YO_BYTES + 4 * TCH + 4 * CPB + 8 * 3 * K * (NPT / 2) * 128 + 4 * NP;
 };
 
 // Load NPT consecutive elements of a staged row as floats (16-byte vector loads).
@@ -219,6 +281,7 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     unsigned* w_spk = reinterpret_cast<unsigned*>(w_pos + kTch);                     // [CPB] MODE 1 spike masks
     // general path, per thread, channel and state pair: (A*log2e), ((n+1)/A), ((n+1) for |A| < 1e-6 else 0)
     float2* w_gen = reinterpret_cast<float2*>(w_spk + CPB);                          // [3][K][NPR][128]
+    float* w_lnp1 = reinterpret_cast<float*>(w_gen + 3 * K * NPR * 128);             // [NP] log(n+1)
 
     const int64_t T_len = MODE ? f.L : a.T, d = MODE ? f.d : a.d, N = MODE ? f.N : a.N;
     const T* p_u = static_cast<const T*>(MODE ? f.x : a.u);
@@ -238,13 +301,18 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     // A = -exp(log_A), rounded like the reference's own tensor op (ssm.py:121).
     // HiPPO structure test, per channel.  fp32 parameters: A[c,n] == (n+1)*A[c,0]
     // to 1e-6 relative.  bf16 parameters: log_A[c,n] == log(n+1) + log_A[c,0] to
-    // one bf16 ulp of the stored value (the HiPPO init up to storage rounding).
+    // one bf16 ulp of the stored value (the HiPPO init up to storage rounding),
+    // tested in the log domain against a per-CTA table of log(n+1), so a HiPPO
+    // channel costs no exponential per state; the general path's per-state
+    // constants are formed only for channels that need them.
     constexpr bool kBf16Params = (MODE == 0 && DT == NT_BF16);
     auto load_logA = [&](int64_t c, int64_t n) -> float {
         if (MODE == 0) return Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.log_A) + c * N + n);
         return f.log_A[c * N + n];
     };
     auto A_of = [&](float la) -> float { return MODE == 0 ? -Elem<DT>::rnd(expf(la)) : -expf(la); };
+    for (int i = tid; i < NP; i += 128) w_lnp1[i] = logf((float)(i + 1));
+    __syncthreads();
     const void* sin = MODE ? (const void*)f.state_in : a.state_in;
     float2 hv[K][NPR];                               // the thread's states, as packed pairs
     float a0l[K], ra0[K], Dv[K];
@@ -260,38 +328,35 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         ra0[k] = 1.0f / Abase;
         Dv[k] = 0.f;
         if (live[k]) Dv[k] = MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + c) : f.Dskip[c];
+        const bool full_slice = live[k] && (int64_t)(sub + 1) * NPT <= N;
+        float hs[NPT];
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) hs[j] = 0.f;
+        if (sin && full_slice) {
+            const int64_t s0 = (b * d + c) * N + (int64_t)sub * NPT;
+            if (MODE == 0 && SDT == NT_BF16) load_state8(static_cast<const __nv_bfloat16*>(sin) + s0, hs);
+            else load_state8(static_cast<const float*>(sin) + s0, hs);
+        }
 #pragma unroll
         for (int j = 0; j < NPT; ++j) {
             const int64_t n = (int64_t)sub * NPT + j;
-            float A = 0.f, h0 = 0.f;
+            float h0 = hs[j];
             const bool on = live[k] && n < N;
             if (on) {
                 const float la = load_logA(c, n);
-                A = A_of(la);
-                if (sin) {
+                if (sin && !full_slice) {
                     const int64_t si = (b * d + c) * N + n;
                     if (MODE == 0 && SDT == NT_BF16) h0 = __bfloat162float(static_cast<const __nv_bfloat16*>(sin)[si]);
                     else h0 = static_cast<const float*>(sin)[si];
                 }
                 if (kBf16Params) {
-                    int e2;
-                    frexpf(la, &e2);                               // |la| in [2^(e2-1), 2^e2)
-                    const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
-                    if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) ok = false;
-                } else if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) {
-                    ok = false;
+                    if (!hippo_state_bf16(la, la0, w_lnp1[n])) ok = false;
+                    if (la <= kLimLogA && fabsf(A_of(la)) < 1e-6f) ok = false;
+                } else {
+                    const float A = A_of(la);
+                    if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A) || fabsf(A) < 1e-6f) ok = false;
                 }
             }
-            const bool lim = on && fabsf(A) < 1e-6f;
-            if (lim) ok = false;
-            // general path on B' = B/(n+1): B_bar*u = (A_bar - 1) * ((n+1)/A) * B' * u,
-            // or dt * (n+1) * B' * u for the |A| < 1e-6 states (ssm.py:129-137)
-            const float np1 = (float)(n + 1);
-            const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
-            const int gi = ((0 * K + k) * NPR + j / 2) * 128 + tid, gs = K * NPR * 128;
-            reinterpret_cast<float*>(w_gen + gi)[j & 1] = A * kLog2e;
-            reinterpret_cast<float*>(w_gen + gi + gs)[j & 1] = ci;
-            reinterpret_cast<float*>(w_gen + gi + 2 * gs)[j & 1] = lim ? np1 : 0.f;
             if (j & 1) hv[k][j / 2].y = h0;
             else hv[k][j / 2].x = h0;
         }
@@ -305,6 +370,26 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
     // the HiPPO path needs every channel of the thread to qualify (else the
     // general path, which is exact for any A, runs for all of them)
     const bool use_hippo = all_hippo;
+    if (!use_hippo) {
+        // general path on B' = B/(n+1): B_bar*u = (A_bar - 1) * ((n+1)/A) * B' * u,
+        // or dt * (n+1) * B' * u for the |A| < 1e-6 states (ssm.py:129-137)
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int64_t n = (int64_t)sub * NPT + j;
+                const bool on = live[k] && n < N;
+                const float A = on ? A_of(load_logA(chan(k), n)) : 0.f;
+                const bool lim = on && fabsf(A) < 1e-6f;
+                const float np1 = (float)(n + 1);
+                const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
+                const int gi = (k * NPR + j / 2) * 128 + tid, gs = K * NPR * 128;
+                reinterpret_cast<float*>(w_gen + gi)[j & 1] = A * kLog2e;
+                reinterpret_cast<float*>(w_gen + gi + gs)[j & 1] = ci;
+                reinterpret_cast<float*>(w_gen + gi + 2 * gs)[j & 1] = lim ? np1 : 0.f;
+            }
+        }
+    }
     float rn[NPT];                                   // 1/(n+1) of the thread's states
 #pragma unroll
     for (int j = 0; j < NPT; ++j) rn[j] = 1.0f / (float)(sub * NPT + j + 1);
@@ -673,43 +758,58 @@ ssm_step_kernel(ScanArgs a) {
     const bool live = c < d;
     const int64_t ld_bc = a.ld_bc > 0 ? a.ld_bc : N;
     const T* logA = static_cast<const T*>(a.log_A) + (live ? c : 0) * N;
+    __shared__ float s_lnp1[NP];
+    for (int i = tid; i < NP; i += kStepThreads) s_lnp1[i] = logf((float)(i + 1));
+    __syncthreads();
     const float la0 = live ? E::load(logA) : 0.f;
     const float Abase = live ? -E::rnd(expf(la0)) : -1.f;
     float2 hv[NPR], A2v[NPR], civ[NPR], lmv[NPR];
+    using ST = typename Elem<SDT>::T;
+    const bool full_slice = live && (int64_t)(sub + 1) * NPT <= N;
+    float hs[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) hs[j] = 0.f;
+    if (a.state_in && full_slice) load_state8(static_cast<const ST*>(a.state_in) + (b * d + c) * N + sub * NPT, hs);
     bool ok = true;
 #pragma unroll
     for (int j = 0; j < NPT; ++j) {
         const int64_t n = (int64_t)sub * NPT + j;
         const bool on = live && n < N;
-        float A = 0.f, h0 = 0.f;
+        float h0 = hs[j];
         if (on) {
             const float la = E::load(logA + n);
-            A = -E::rnd(expf(la));
-            if (a.state_in) {
+            if (a.state_in && !full_slice) {
                 const int64_t si = (b * d + c) * N + n;
                 h0 = SDT == NT_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.state_in)[si])
                                     : static_cast<const float*>(a.state_in)[si];
             }
             if (DT == NT_BF16) {
-                int e2;
-                frexpf(la, &e2);
-                const float ulp = la == 0.f ? 0.f : ldexpf(1.f, e2 - 8);
-                if (fabsf(la - (logf((float)(n + 1)) + la0)) > ulp) ok = false;
-            } else if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A)) {
-                ok = false;
+                if (!hippo_state_bf16(la, la0, s_lnp1[n])) ok = false;
+                if (la <= kLimLogA && fabsf(E::rnd(expf(la))) < 1e-6f) ok = false;
+            } else {
+                const float A = -E::rnd(expf(la));
+                if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A) || fabsf(A) < 1e-6f) ok = false;
             }
         }
-        const bool lim = on && fabsf(A) < 1e-6f;
-        if (lim) ok = false;
-        const float np1 = (float)(n + 1);
-        const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
-        float* hp = (j & 1) ? &hv[j / 2].y : &hv[j / 2].x;
-        *hp = h0;
-        if (j & 1) { A2v[j / 2].y = A * kLog2e; civ[j / 2].y = ci; lmv[j / 2].y = lim ? np1 : 0.f; }
-        else { A2v[j / 2].x = A * kLog2e; civ[j / 2].x = ci; lmv[j / 2].x = lim ? np1 : 0.f; }
+        if (j & 1) hv[j / 2].y = h0;
+        else hv[j / 2].x = h0;
     }
     const unsigned okm = __ballot_sync(0xffffffffu, ok);
     const bool hippo = (okm & gmask) == gmask;
+    if (!hippo) {
+        // the general path's per-state constants (only channels that need them pay for the exponentials)
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int64_t n = (int64_t)sub * NPT + j;
+            const bool on = live && n < N;
+            const float A = on ? -E::rnd(expf(E::load(logA + n))) : 0.f;
+            const bool lim = on && fabsf(A) < 1e-6f;
+            const float np1 = (float)(n + 1);
+            const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
+            if (j & 1) { A2v[j / 2].y = A * kLog2e; civ[j / 2].y = ci; lmv[j / 2].y = lim ? np1 : 0.f; }
+            else { A2v[j / 2].x = A * kLog2e; civ[j / 2].x = ci; lmv[j / 2].x = lim ? np1 : 0.f; }
+        }
+    }
     const float a0l = Abase * kLog2e, ra0 = 1.0f / Abase;
     const float np1a = (float)(sub * NPT + 1), np1b = (float)(sub * NPT + 2);
     const float Dv = live ? E::load(static_cast<const T*>(a.D) + c) : 0.f;
@@ -776,14 +876,20 @@ ssm_step_kernel(ScanArgs a) {
         }
     }
     if (a.state_out && live) {
+        float ho[NPT];
 #pragma unroll
-        for (int j = 0; j < NPT; ++j) {
-            const int64_t n = (int64_t)sub * NPT + j;
-            if (n >= N) continue;
-            const int64_t si = (b * d + c) * N + n;
-            const float hj = (j & 1) ? hv[j / 2].y : hv[j / 2].x;
-            if (SDT == NT_BF16) static_cast<__nv_bfloat16*>(a.state_out)[si] = __float2bfloat16_rn(hj);
-            else static_cast<float*>(a.state_out)[si] = hj;
+        for (int j = 0; j < NPT; ++j) ho[j] = (j & 1) ? hv[j / 2].y : hv[j / 2].x;
+        if (full_slice) {
+            store_state8(static_cast<ST*>(a.state_out) + (b * d + c) * N + sub * NPT, ho);
+        } else {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int64_t n = (int64_t)sub * NPT + j;
+                if (n >= N) continue;
+                const int64_t si = (b * d + c) * N + n;
+                if (SDT == NT_BF16) static_cast<__nv_bfloat16*>(a.state_out)[si] = __float2bfloat16_rn(ho[j]);
+                else static_cast<float*>(a.state_out)[si] = ho[j];
+            }
         }
     }
 }

@@ -239,3 +239,69 @@ def test_forward_in_sequence_groups_matches_one_pass():
         close(s1.ssm_state, s2.ssm_state)
     assert last.shape == (5, 1, 1000)
     torch.testing.assert_close(last[:, 0].float(), lg2b[:, -1].float(), rtol=2e-2, atol=2e-2)
+
+
+def test_checkpoint_round_trip_and_cache_invalidation(tmp_path):
+    """save -> from_checkpoint -> forward gives the same logits, states and
+    metrics as the engine that saved it (engine.py:90-103,267-272); a checkpoint
+    written by the reference's own engine loads too; and load_state_dict into a
+    live model invalidates the packed-weight caches (the next forward uses the
+    new weights, equal to a fresh engine built from them)."""
+    from neuratensor_b200 import InferenceEngine, ModelConfig, NeuraTensorModel
+    torch.manual_seed(31)
+    cfg = ModelConfig(vocab_size=500, d_model=64, n_layers=3, d_state=8, max_seq_len=256, attn_every=3,
+                      attn_heads=1, attn_window=32)
+    eng = InferenceEngine(NeuraTensorModel(cfg), device=DEV, dtype=torch.bfloat16)
+    ids = torch.randint(0, 500, (2, 40))
+    r1 = eng.run(ids, reset_state=True)
+    path = str(tmp_path / "ckpt.pt")
+    eng.save(path)
+    eng2 = InferenceEngine.from_checkpoint(path, device=DEV, dtype=torch.bfloat16)
+    r2 = eng2.run(ids, reset_state=True)
+    assert torch.equal(r1.logits, r2.logits)
+    assert r1.metrics == r2.metrics
+    for a, b in zip(r1.states, r2.states):
+        assert torch.equal(a.membrane, b.membrane) and torch.equal(a.ssm_state, b.ssm_state)
+
+    # new weights into the live model: caches keyed on parameter storage and version are rebuilt
+    torch.manual_seed(32)
+    other = NeuraTensorModel(cfg)
+    eng.model.load_state_dict(other.state_dict())
+    r3 = eng.run(ids, reset_state=True)
+    eng3 = InferenceEngine(other, device=DEV, dtype=torch.bfloat16)
+    r4 = eng3.run(ids, reset_state=True)
+    assert not torch.equal(r3.logits, r1.logits)
+    assert torch.equal(r3.logits, r4.logits)
+    # an in-place edit of one parameter bumps its version and is picked up as well
+    with torch.no_grad():
+        eng.model.blocks[0].out_scale.mul_(2)
+        eng3.model.blocks[0].out_scale.mul_(2)
+    assert torch.equal(eng.run(ids, reset_state=True).logits, eng3.run(ids, reset_state=True).logits)
+
+
+def test_checkpoint_from_the_reference_engine_loads(tmp_path):
+    """A checkpoint the reference's own InferenceEngine.save wrote (its ModelConfig
+    class inside) loads into this engine and reproduces the reference's pico golden."""
+    import importlib
+    import os
+    import sys
+    from conftest import ROOT
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "neuratensor")):
+        pytest.skip("reference package not installed at baseline/_ref")
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    nt = importlib.import_module("neuratensor")
+    from neuratensor.config.presets import get_preset as ref_preset
+    from neuratensor.core.model import NeuraTensorModel as RefModel
+    from neuratensor.inference.engine import InferenceEngine as RefEngine
+    from neuratensor_b200 import InferenceEngine
+    torch.manual_seed(0)
+    ref_eng = RefEngine(RefModel(ref_preset("pico")), device="cpu", dtype=torch.float32)
+    path = str(tmp_path / "ref.pt")
+    ref_eng.save(path)
+    eng = InferenceEngine.from_checkpoint(path, device=DEV, dtype=torch.float32)
+    d = load_golden("pico_fp32.npz")
+    res = eng.run(torch.from_numpy(d["ids"]), reset_state=True)
+    np.testing.assert_allclose(N(res.logits[0, d["logits_row_idx"]]), d["logits_rows"], rtol=1e-4, atol=1e-5)
+    assert nt.__version__ == "4.0.4"

@@ -29,6 +29,7 @@
  *   nt_attention_forward   SlidingWindowAttention.forward neuratensor/core/model.py:148-181
  *   nt_embedding           NeuraTensorModel.embedding  neuratensor/core/model.py:258
  *   nt_lm_head             NeuraTensorModel.norm + lm_head neuratensor/core/model.py:283-284
+ *   nt_greedy_tokens       top-k = 1 sampling in NeuraTensorModel.generate model.py:344-359
  *   nt_lif_ssm_fused       LIF spikes driving the selective scan with given dt/B/C
  *                          (snn.py:167-182 feeding ssm.py:106-139,184-221)
  *
@@ -189,6 +190,15 @@ NT_API int nt_attention_forward(int dtype, int64_t B, int64_t T, int64_t dm, int
  * raises IndexError. */
 NT_API int nt_embedding(int dtype, int64_t M, int64_t dm, int64_t vocab, const int64_t* ids, const void* W,
                         void* out, void* stream);
+
+/* Greedy next tokens -- NeuraTensorModel.generate with top_k = 1, temperature 1,
+ * top_p 1 and no repetition penalty (model.py:344-359): per row of logits
+ * [B, vocab] (row stride ld elements, `dtype`), the reference keeps the entries
+ * equal to the maximum and samples among them; this picks the
+ * floor(u[r] * ties)-th tied index in index order, u: [B] float32 in [0, 1).
+ * tokens: [B] int64 device output. */
+NT_API int nt_greedy_tokens(int dtype, int64_t B, int64_t vocab, const void* logits, int64_t ld, const float* u,
+                            int64_t* tokens, void* stream);
 
 /* Final RMSNorm + tied lm_head -- NeuraTensorModel.norm + lm_head
  * (model.py:283-284): logits = RMSNorm(x) W^T, logits in `dtype` (bf16 logits

@@ -47,11 +47,20 @@ def _deps_mtime() -> float:
 
 
 def up_to_date() -> bool:
-    """The library is newer than every source, header and object it is made of."""
+    """Every object is newer than its source and every header, and the library
+    newer than every source, header and object."""
     if not os.path.exists(LIB):
         return False
-    objs = [os.path.join(BUILD, f) for f in os.listdir(BUILD)] if os.path.isdir(BUILD) else []
-    newest = max([_deps_mtime()] + [os.path.getmtime(o) for o in objs if o.endswith(".o")])
+    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if not f.endswith(".cu")] + \
+        [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE)]
+    hdr = max(os.path.getmtime(p) for p in headers)
+    objs = []
+    for src in sources():
+        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        if not os.path.exists(obj) or os.path.getmtime(obj) < max(os.path.getmtime(src), hdr):
+            return False
+        objs.append(obj)
+    newest = max([_deps_mtime()] + [os.path.getmtime(o) for o in objs])
     return os.path.getmtime(LIB) >= newest
 
 

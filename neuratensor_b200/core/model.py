@@ -327,7 +327,14 @@ class NeuraTensorModel(nn.Module):
         if use_graph and out.is_cuda and max_new_tokens > 1:
             graph = self.decode_graph(out.shape[0], out.device, logits.dtype)
             graph.load_states(states)
-        for _ in range(max_new_tokens):
+        # top_k = 1 without nucleus filtering leaves the tied row maxima with
+        # equal probability: one kernel picks among them with a uniform drawn
+        # here for every step at once (the other filters run as written)
+        greedy = out.is_cuda and top_k == 1 and top_p >= 1.0
+        if greedy:
+            from .. import native
+            u_all = torch.rand((max_new_tokens, out.shape[0]), device=out.device)
+        for step in range(max_new_tokens):
             if repetition_penalty != 1.0:
                 for b in range(out.shape[0]):
                     for tok in out[b].tolist():
@@ -335,7 +342,9 @@ class NeuraTensorModel(nn.Module):
                         nxt_logits[b, tok] = v / repetition_penalty if v > 0 else v * repetition_penalty
             if temperature != 1.0:
                 nxt_logits = nxt_logits / temperature
-            if top_k > 0:
+            if greedy:
+                tok = native.greedy_tokens(nxt_logits, u_all[step])
+            elif top_k > 0:
                 kth = torch.topk(nxt_logits, min(top_k, nxt_logits.size(-1))).values[:, [-1]]
                 nxt_logits[nxt_logits < kth] = float("-inf")
             if top_p < 1.0:
@@ -344,7 +353,8 @@ class NeuraTensorModel(nn.Module):
                 drop = p.cumsum(-1) - p > top_p
                 srt = srt.masked_fill(drop, float("-inf"))
                 nxt_logits = torch.zeros_like(nxt_logits).scatter_(-1, idx, srt)
-            tok = torch.multinomial(torch.softmax(nxt_logits, dim=-1), num_samples=1)
+            if not greedy:
+                tok = torch.multinomial(torch.softmax(nxt_logits, dim=-1), num_samples=1)
             out = torch.cat([out, tok], dim=1)
             if stop and tok.item() in stop:
                 break

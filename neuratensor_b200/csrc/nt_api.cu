@@ -357,6 +357,15 @@ int nt_embedding(int dtype, int64_t M, int64_t dm, int64_t vocab, const int64_t*
     return launch_embedding(dtype, M, dm, vocab, ids, W, out, as_stream(stream));
 }
 
+int nt_greedy_tokens(int dtype, int64_t B, int64_t vocab, const void* logits, int64_t ld, const float* u,
+                     int64_t* tokens, void* stream) {
+    if (!act_dtype_ok(dtype)) return fail(NT_ERR_DTYPE, "nt_greedy_tokens: dtype %d", dtype);
+    if (B < 0 || vocab < 1 || ld < vocab || B > 2147483647LL) return fail(NT_ERR_ARG, "nt_greedy_tokens: bad sizes");
+    if (B == 0) return NT_OK;
+    if (!logits || !u || !tokens) return fail(NT_ERR_ARG, "nt_greedy_tokens: null pointer");
+    return launch_greedy(dtype, B, vocab, logits, ld, u, tokens, as_stream(stream));
+}
+
 int64_t nt_lm_head_workspace_bytes(int dtype, int64_t M, int64_t dm, int64_t vocab) {
     (void)vocab;
     return align256(M * dm * esize(dtype));

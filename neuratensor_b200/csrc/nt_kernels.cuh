@@ -63,6 +63,10 @@ int launch_rmsnorm(int dtype, int64_t M, int64_t D, const void* x, const void* w
 int launch_embedding(int dtype, int64_t M, int64_t D, int64_t vocab, const int64_t* ids, const void* W, void* out,
                      cudaStream_t stream);
 
+// Greedy choice per row of logits [B, V] (row stride ld): uniform among the tied maxima, u[r] in [0,1).
+int launch_greedy(int dtype, int64_t B, int64_t V, const void* logits, int64_t ld, const float* u, int64_t* out,
+                  cudaStream_t stream);
+
 // Row compaction (the density decision of _sparse_out_proj): counters[0] =
 // n_active, counters[1] = 1 when the sparse branch is taken (2*n_active <= M),
 // counters[2] = rows the out_proj GEMM processes.  Only on the sparse branch

@@ -351,8 +351,8 @@ lif_short_kernel(LifArgs a) {
     if (a.row_bits) {
         if (lane == 0) s_bits[warp] = bits;
         __syncthreads();
-        // warps 2k and 2k+1 hold the 64 channels of block blockIdx.x*4 + k
-        const int64_t cblk = (int64_t)blockIdx.x * 4 + (tid >> 1);
+        // warps 2k and 2k+1 hold the 64 channels of block blockIdx.x*4 + k; thread k writes it
+        const int64_t cblk = (int64_t)blockIdx.x * 4 + tid;
         if (tid < 4 && cblk * kLifChannels < a.C)
             a.row_bits[(cblk * a.B + b) * a.n_words] = s_bits[2 * tid] | s_bits[2 * tid + 1];
     }

@@ -140,6 +140,84 @@ int launch_embedding(int dtype, int64_t M, int64_t D, int64_t vocab, const int64
 }
 
 // ---------------------------------------------------------------------------
+// Greedy token choice (model.py:344-359 with top_k = 1): the reference keeps
+// every logit equal to the row maximum (`logits < topk(logits, 1)[-1]` ->
+// -inf), softmaxes and samples, i.e. picks uniformly among the tied maxima.
+// One CTA per row: the maximum and the number of positions holding it, then
+// the floor(u * ties)-th of them in index order (u in [0, 1) per row, from the
+// caller's generator).  NaN logits compare false, as in torch's `<`.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) greedy_kernel(int64_t V, const T* logits, int64_t ld, const float* u,
+                                                      int64_t* out) {
+    __shared__ float s_red[8];
+    __shared__ int s_cnt[8];
+    __shared__ int s_pick;
+    const int64_t r = blockIdx.x;
+    const T* row = logits + r * ld;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    auto at = [&](int64_t i) -> float {
+        if constexpr (sizeof(T) == 2) return __bfloat162float(row[i]);
+        else return row[i];
+    };
+    float m = -INFINITY;
+    for (int64_t i = tid; i < V; i += 256) m = fmaxf(m, at(i));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_red[warp] = m;
+    __syncthreads();
+    m = s_red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, s_red[w]);
+    // ties, counted per thread over a contiguous slice so that the k-th tie in
+    // index order can be located with one prefix over the 256 counts
+    const int64_t per = (V + 255) / 256, lo = tid * per, hi = lo + per < V ? lo + per : V;
+    int cnt = 0;
+    for (int64_t i = lo; i < hi; ++i) cnt += at(i) == m;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_cnt[warp] = incl;
+    __syncthreads();
+    int base = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        if (w < warp) base += s_cnt[w];
+        total += s_cnt[w];
+    }
+    const int excl = base + incl - cnt;
+    if (tid == 0) s_pick = -1;
+    __syncthreads();
+    int k = total > 0 ? (int)(u[r] * (float)total) : 0;
+    if (k >= total) k = total - 1;
+    if (cnt > 0 && k >= excl && k < excl + cnt) {
+        int seen = excl;
+        for (int64_t i = lo; i < hi; ++i)
+            if (at(i) == m) {
+                if (seen == k) { out[r] = i; break; }
+                ++seen;
+            }
+        s_pick = 1;
+    }
+    __syncthreads();
+    if (tid == 0 && s_pick < 0) out[r] = 0;              // no comparable logit (all NaN)
+}
+
+int launch_greedy(int dtype, int64_t B, int64_t V, const void* logits, int64_t ld, const float* u, int64_t* out,
+                  cudaStream_t stream) {
+    if (dtype == NT_F32)
+        greedy_kernel<float><<<(unsigned)B, 256, 0, stream>>>(V, static_cast<const float*>(logits), ld, u, out);
+    else if (dtype == NT_BF16)
+        greedy_kernel<__nv_bfloat16><<<(unsigned)B, 256, 0, stream>>>(V, static_cast<const __nv_bfloat16*>(logits),
+                                                                       ld, u, out);
+    else return fail(NT_ERR_DTYPE, "greedy: dtype %d", dtype);
+    return check_launch("greedy_kernel");
+}
+
+// ---------------------------------------------------------------------------
 // flags[r] = any(spikes[r, :] != 0).  One warp per row, 16-byte loads when
 // the row is 16-byte aligned; a value is non-zero when its magnitude bits
 // are (so -0.0 counts as zero, as in torch's `any`).

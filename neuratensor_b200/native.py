@@ -57,6 +57,7 @@ _SIGS = {
     "nt_lif_ssm_fused": ([_I64, _I64, _I64, _I64] + [_P] * 14 + [_I32, _P, _P], _I32),
     "nt_window_attention": ([_I32, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _I64, _P], _I32),
     "nt_embedding": ([_I32, _I64, _I64, _I64, _P, _P, _P, _P], _I32),
+    "nt_greedy_tokens": ([_I32, _I64, _I64, _P, _I64, _P, _P, _P], _I32),
     "nt_attention_workspace_bytes": ([_I32, _I64, _I64, _I64], _I64),
     "nt_attention_forward": ([_I32, _I64, _I64, _I64, _I64, _I64] + [_P] * 8 + [_I64, _P], _I32),
     "nt_lm_head_workspace_bytes": ([_I32, _I64, _I64, _I64], _I64),
@@ -390,6 +391,23 @@ def attention_forward(x: Tensor, norm_w: Tensor, W_qkv: Tensor, W_o: Tensor, n_h
     return out
 
 
+def greedy_tokens(logits: Tensor, u: Tensor, out: Optional[Tensor] = None) -> Tensor:
+    """top_k = 1 sampling of generate (model.py:344-359): per row of logits [B, V],
+    uniformly among the entries equal to the row maximum, chosen by u [B] in [0, 1).
+    Returns int64 tokens [B, 1] (written into `out` when given)."""
+    dev = _require_cuda(logits, u)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be [B, V] with unit column stride")
+    B, V = logits.shape
+    u = _c(u, torch.float32)
+    if out is None:
+        out = torch.empty((B, 1), dtype=torch.int64, device=dev)
+    rc = load().nt_greedy_tokens(_dtype_code(logits), B, V, _p(logits), logits.stride(0), _p(u), _p(out),
+                                 _stream(dev))
+    _check("nt_greedy_tokens", rc)
+    return out
+
+
 def embedding(ids: Tensor, W: Tensor) -> Tensor:
     """nn.Embedding lookup (model.py:258): ids [...] int64 -> [..., d_model] in W's dtype.
     An id outside [0, vocab) gives a zero row and a flag in the device error word."""
@@ -403,15 +421,22 @@ def embedding(ids: Tensor, W: Tensor) -> Tensor:
     return out
 
 
-def lm_head(x: Tensor, gamma: Tensor, W: Tensor, workspace: Optional[Tensor] = None) -> Tensor:
-    """Final RMSNorm + tied lm_head (model.py:283-284): x [..., dm] -> logits [..., vocab] in x.dtype."""
+def lm_head(x: Tensor, gamma: Tensor, W: Tensor, workspace: Optional[Tensor] = None,
+            out: Optional[Tensor] = None) -> Tensor:
+    """Final RMSNorm + tied lm_head (model.py:283-284): x [..., dm] -> logits [..., vocab] in x.dtype
+    (written into `out`, a contiguous tensor of that shape, when given)."""
     dev = _require_cuda(x, gamma, W)
     a = x.dtype
     dm = x.shape[-1]
     vocab = W.shape[0]
     M = x.numel() // dm
     x2, g2, W2 = _c(x), _c(gamma, a), _c(W, a)
-    logits = torch.empty((*x.shape[:-1], vocab), dtype=a, device=dev)
+    if out is not None:
+        if out.dtype != a or not out.is_contiguous() or out.numel() != M * vocab:
+            raise ValueError("out must be a contiguous [..., vocab] tensor in x.dtype")
+        logits = out
+    else:
+        logits = torch.empty((*x.shape[:-1], vocab), dtype=a, device=dev)
     L = load()
     nbytes = L.nt_lm_head_workspace_bytes(_DT[a], M, dm, vocab)
     ws = workspace if (workspace is not None and workspace.numel() >= nbytes) else _workspace(nbytes, dev)

@@ -480,7 +480,8 @@ def test_block_forward_short_sequences_sparse_branch(nat, Tn):
     B = 16
     x = rng.normal(0, 1.0, (B, Tn, 64)).astype(np.float32)
     mem0 = rng.normal(0, 0.1, (B, 128)).astype(np.float32)
-    mem0[np.arange(5), np.arange(5)] = 1.2              # rows (b < 5, t = 0) spike, the rest stay silent
+    # rows (b < 5, t = 0) spike, in channels of both 64-channel blocks; the rest stay silent
+    mem0[np.arange(5), np.arange(5) + 64 * (np.arange(5) % 2)] = 1.2
     st0 = rng.normal(0, 0.3, (B, 128, 16)).astype(np.float32)
     cap = {}
     ro, rst, rm = O.block_forward(x, p, O.OracleState(mem0, st0), "fp32", capture=cap)
@@ -544,6 +545,66 @@ def test_embedding_bad_id_flags_and_zeroes(nat):
     assert torch.count_nonzero(out[0, 1:3]).item() == 0
     assert nat.device_error_flags(0) == 8                   # ERRF_BAD_ARG, then cleared
     assert nat.device_error_flags(0) == 0
+
+
+def _greedy_ref(logits, u):
+    """top_k = 1 as generate does it (model.py:344-359): the entries equal to the
+    row maximum survive with equal probability; u picks the floor(u * ties)-th."""
+    out = []
+    for row, ur in zip(logits, u):
+        m = row.max()
+        ties = np.flatnonzero(row == m)
+        out.append(int(ties[min(int(np.float32(ur) * np.float32(len(ties))), len(ties) - 1)]) if len(ties) else 0)
+    return np.asarray(out)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_greedy_tokens_exact(nat, dtype):
+    g = torch.Generator(device=DEV).manual_seed(5)
+    B, V = 37, 32000
+    logits = torch.randn(B, V, device=DEV, generator=g).to(dtype)
+    # planted ties: rows with 2, 3 and 7 equal maxima, one all-equal row, one -inf row mix
+    logits[1, [5, 900, 31999]] = 50.0
+    logits[2, [0, 1]] = 60.0
+    logits[3, ::4571] = 70.0
+    logits[4] = 1.0
+    logits[5, :] = float("-inf")
+    logits[5, 17] = -3.0
+    u = torch.rand(B, device=DEV, generator=g)
+    u[1], u[2], u[3], u[4] = 0.999999, 0.5, 0.0, 0.73
+    tok = nat.greedy_tokens(logits, u)
+    assert tok.shape == (B, 1) and tok.dtype == torch.int64
+    ref = _greedy_ref(logits.float().cpu().numpy(), u.cpu().numpy())
+    np.testing.assert_array_equal(tok[:, 0].cpu().numpy(), ref)
+    assert tok[1, 0].item() == 31999 and tok[2, 0].item() == 1 and tok[3, 0].item() == 0
+    assert tok[4, 0].item() == int(0.73 * V) and tok[5, 0].item() == 17
+    # a strided view (the last position of [B, T, V] logits) and a small vocab
+    big = torch.randn(3, 4, 1000, device=DEV, generator=g).to(dtype)
+    u3 = torch.rand(3, device=DEV, generator=g)
+    got = nat.greedy_tokens(big[:, -1, :], u3)
+    np.testing.assert_array_equal(got[:, 0].cpu().numpy(), _greedy_ref(big[:, -1].float().cpu().numpy(),
+                                                                         u3.cpu().numpy()))
+
+
+def test_generate_top1_matches_argmax_path(nat):
+    """generate(top_k=1) takes the greedy kernel inside the captured decode loop;
+    with no ties in the logits its tokens equal the argmax chain of the
+    carried-state step-by-step forward (the same kernels, launched one by one)."""
+    from neuratensor_b200 import NeuraTensorModel, get_preset
+    torch.manual_seed(0)
+    model = NeuraTensorModel(get_preset("pico")).to(DEV).eval()
+    ids = torch.randint(0, model.config.vocab_size, (2, 12), device=DEV)
+    before = nat.launch_count()
+    out, _ = model.generate(ids, max_new_tokens=6, top_k=1)
+    assert nat.launch_count() > before
+    chain = ids
+    with torch.no_grad():
+        lg, st, _ = model.forward_device(ids, None, last_only=True)
+        for _ in range(6):
+            tok = lg[:, -1].argmax(-1, keepdim=True)
+            chain = torch.cat([chain, tok], 1)
+            lg, st, _ = model.forward_device(tok, st)
+    assert torch.equal(out, chain)
 
 
 def test_bounded_wait_expires_into_the_error_word(nat):

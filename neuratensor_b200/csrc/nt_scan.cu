@@ -328,10 +328,10 @@ ssm_scan_kernel(ScanArgs a, FusedArgs f) {
         ra0[k] = 1.0f / Abase;
         Dv[k] = 0.f;
         if (live[k]) Dv[k] = MODE == 0 ? Elem<DT>::load(static_cast<const typename Elem<DT>::T*>(a.D) + c) : f.Dskip[c];
-        const bool full_slice = live[k] && (int64_t)(sub + 1) * NPT <= N;
-        float hs[NPT];
+        const bool full_slice = NPT == 8 && live[k] && (int64_t)(sub + 1) * NPT <= N;
+        float hs[8];
 #pragma unroll
-        for (int j = 0; j < NPT; ++j) hs[j] = 0.f;
+        for (int j = 0; j < 8; ++j) hs[j] = 0.f;
         if (sin && full_slice) {
             const int64_t s0 = (b * d + c) * N + (int64_t)sub * NPT;
             if (MODE == 0 && SDT == NT_BF16) load_state8(static_cast<const __nv_bfloat16*>(sin) + s0, hs);
@@ -688,6 +688,9 @@ int launch_tpc(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
 #ifndef NT_SCAN_WIDE_WARPS
 #define NT_SCAN_WIDE_WARPS 6
 #endif
+#ifndef NT_SCAN_NARROW_WARPS
+#define NT_SCAN_NARROW_WARPS 2
+#endif
 // Slicing: 8 states per thread (TPC = N/8 threads per channel).  Two channels
 // per thread (their B and C slices loaded once) when that still leaves every
 // SM sub-partition NT_SCAN_WIDE_WARPS warps or more: the recurrence of one
@@ -704,6 +707,19 @@ int launch_mode(const ScanArgs& a, const FusedArgs& f, cudaStream_t stream) {
     // (bf16 inputs only: the float32 path is the parity configuration)
     const bool wide = (MODE == 1 || DT == NT_BF16) && OUT == 1 && tpc <= 16 &&
                       warps2 >= (int64_t)NT_SCAN_WIDE_WARPS * 4 * sms;
+    if constexpr (MODE == 0 && DT == NT_BF16 && OUT == 1) {
+        // fewer than two warps per SM sub-partition with 8 states per thread:
+        // 4 states per thread doubles the warps (d_state <= 32 only)
+        const int64_t warps1 = B * ((d + 128 / tpc - 1) / (128 / tpc)) * 4;
+        if (N > 4 && N <= 32 && warps1 < (int64_t)NT_SCAN_NARROW_WARPS * 4 * sms) {
+            switch (pow2_at_least((N + 3) / 4)) {
+                case 2: return launch_tpc<DT, SDT, MODE, 2, 4, 1, OUT>(a, f, stream);
+                case 4: return launch_tpc<DT, SDT, MODE, 4, 4, 1, OUT>(a, f, stream);
+                case 8: return launch_tpc<DT, SDT, MODE, 8, 4, 1, OUT>(a, f, stream);
+                default: break;
+            }
+        }
+    }
     if constexpr (MODE == 1 || (DT == NT_BF16 && OUT == 1)) {
       if (wide) {
         switch (tpc) {
@@ -744,7 +760,7 @@ constexpr int kStepMaxT = 4;
 constexpr int kStepThreads = 256;
 
 template <int DT, int SDT, int TPC>
-__global__ void __launch_bounds__(kStepThreads)
+__global__ void __launch_bounds__(kStepThreads, 4)
 ssm_step_kernel(ScanArgs a) {
     using E = Elem<DT>;
     using T = typename E::T;

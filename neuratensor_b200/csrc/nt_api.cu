@@ -3,6 +3,7 @@
 // point replaces are in include/neuratensor_native.h.
 #include "nt_kernels.cuh"
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstring>
@@ -120,6 +121,8 @@ struct BlockWs {
     int *pos, *idx, *counters;
     void* scanseg;              // float32 end states / decays / carry-ins of the segmented scan
     size_t scanseg_bytes;
+    float* part;                // split-K partial sums of the block's GEMMs (small row counts)
+    int64_t part_elems;
     int64_t bytes;
 };
 BlockWs block_ws(void* ws, int dtype, int64_t B, int64_t T, int64_t dm, int64_t di, int64_t N) {
@@ -140,6 +143,15 @@ BlockWs block_ws(void* ws, int dtype, int64_t B, int64_t T, int64_t dm, int64_t 
     w.counters = c.take<int>(64);
     w.scanseg_bytes = selective_scan_segmented_workspace(B, T, di, N);
     w.scanseg = w.scanseg_bytes ? c.take<char>((int64_t)w.scanseg_bytes) : nullptr;
+    w.part_elems = 0;
+    if (dtype == NT_BF16) {
+        const int64_t shapes[3][3] = {{2 * di, dm}, {di + 2 * N, di}, {dm, di}};   // N, K of each GEMM
+        for (const auto& sh : shapes) {
+            const int s = gemm_split_k(M, sh[0], sh[1]);
+            if (s > 1) w.part_elems = std::max<int64_t>(w.part_elems, (int64_t)s * M * sh[0]);
+        }
+    }
+    w.part = w.part_elems ? c.take<float>(w.part_elems * (int64_t)sizeof(float)) : nullptr;
     w.bytes = c.off;
     return w;
 }
@@ -431,7 +443,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         g.M = M; g.N = 2 * di; g.K = dm;
         g.A = w.xn; g.lda = dm; g.Bw = W_in; g.ldb = dm;
         g.epi.kind = EPI_SPLIT2_SILU; g.epi.out = w.h; g.epi.ldo = di; g.epi.out2 = w.gate; g.epi.ldo2 = di;
-        g.epi.split = di;
+        g.epi.split = di; g.part = w.part; g.part_elems = w.part_elems;
         NT_TRY(launch_gemm(dtype, g, st));
     }
     // (a) LIF -> spikes, membrane, row-activity bits
@@ -449,7 +461,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         g.M = M; g.N = di + 2 * N; g.K = di;
         g.A = w.spikes; g.lda = di; g.Bw = W_proj; g.ldb = di;
         g.epi.kind = EPI_SSM_PROJ; g.epi.out = w.dt; g.epi.ldo = di; g.epi.out2 = w.bc; g.epi.ldo2 = 2 * N;
-        g.epi.split = di; g.epi.bias = b_dt;
+        g.epi.split = di; g.epi.bias = b_dt; g.part = w.part; g.part_elems = w.part_elems;
         NT_TRY(launch_gemm(dtype, g, st));
     }
     // (b) selective scan with the gate fused, rows compacted when sparse
@@ -466,6 +478,7 @@ int nt_block_forward(int dtype, int state_dtype, int64_t B, int64_t T, int64_t d
         g.A = w.o; g.lda = di; g.Bw = W_out; g.ldb = di; g.m_count = w.counters + 2;
         g.epi.kind = EPI_OUT_PROJ; g.epi.out = out; g.epi.ldo = dm; g.epi.scale = out_scale; g.epi.resid = x;
         g.epi.ldr = dm; g.epi.row_idx = w.idx; g.epi.row_sparse = w.counters + 1;
+        g.part = w.part; g.part_elems = w.part_elems;
         NT_TRY(launch_gemm(dtype, g, st));
     }
     // rows skipped by the sparse branch: out = 0 * out_scale + x = x

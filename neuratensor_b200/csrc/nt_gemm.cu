@@ -16,6 +16,7 @@
 #include "nt_kernels.cuh"
 
 #include <cuda.h>
+#include <algorithm>
 #include <mutex>
 
 namespace nt {
@@ -278,7 +279,8 @@ template <int BN> struct TcStages {
 template <int KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-               int64_t M, int64_t N, int64_t K, const int* m_count, EpiArgs epi, unsigned* err) {
+               int64_t M, int64_t N, int64_t K, const int* m_count, EpiArgs epi, unsigned* err, int splits,
+               float* partials) {
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= kAccStride, "tile width");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte alignment for the swizzled tiles
@@ -290,7 +292,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int n_tiles = (int)((N + BN - 1) / BN);
     const int total = m_tiles * n_tiles;
     const int nk = (int)((K + kBK - 1) / kBK);
-    if ((int)blockIdx.x >= total) return;
+    // work items: (tile, K split); split s covers k-blocks [s*nk/splits, (s+1)*nk/splits),
+    // never empty (splits <= nk), and with splits > 1 the epilogue writes float32
+    // partial sums for gemm_splitk_epi_kernel instead of the outputs
+    const int items = total * splits;
+    if ((int)blockIdx.x >= items) return;
 
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&map_a);
@@ -321,9 +327,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             constexpr uint32_t bytes = (uint32_t)((kBM + BN) * kBK * sizeof(__nv_bfloat16));
             int it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+                const int tile = item / splits, sp = item % splits;
+                const int kb0 = (int)((int64_t)sp * nk / splits), kb1 = (int)((int64_t)(sp + 1) * nk / splits);
                 const int m0 = (tile / n_tiles) * kBM, n0 = (tile % n_tiles) * BN;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % STAGES;
                     if (it >= STAGES && !mbar_wait(smem_u32(&S.empty[s]), ((it / STAGES) - 1) & 1)) {
                         atomicOr(err, ERRF_TIMEOUT_PRODUCER);
@@ -342,7 +350,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             constexpr uint32_t idesc = idesc_bf16(kBM, BN);
             int it = 0, local = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++local) {
+            for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++local) {
+                const int sp = item % splits;
+                const int kb0 = (int)((int64_t)sp * nk / splits), kb1 = (int)((int64_t)(sp + 1) * nk / splits);
                 const int buf = local & 1;
                 if (local >= 2 && !mbar_wait(smem_u32(&S.acc_empty[buf]), ((local >> 1) - 1) & 1)) {
                     atomicOr(err, ERRF_TIMEOUT_MMA);
@@ -350,7 +360,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * kAccStride);
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % STAGES;
                     if (!mbar_wait(smem_u32(&S.full[s]), (it / STAGES) & 1)) {
                         atomicOr(err, ERRF_TIMEOUT_MMA);
@@ -363,7 +373,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     for (int k = 0; k < kBK / 16; ++k) {
                         // advance 16 bf16 (32 bytes) along K inside the swizzle atom
                         tc_mma(d, sw128_kmajor_desc(sa + k * 32), sw128_kmajor_desc(sb + k * 32), idesc,
-                               (kb | k) ? 1u : 0u);
+                               (kb != kb0 || k) ? 1u : 0u);
                     }
                     tc_commit(smem_u32(&S.empty[s]));
                 }
@@ -373,12 +383,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     } else {
         // ---------------- epilogue: TMEM -> registers -> global ----------------
         constexpr int kParts = kEpiWarps / 4;      // warps sharing a lane quarter
+        constexpr int kChunks = (BN / 16 + kParts - 1) / kParts;   // 16-column chunks per warp, at most
         const int q = warp & 3;                     // TMEM lane quarter this warp may access
         const int part = (warp - 2) >> 2;           // its 16-column chunks: part, part + kParts, ...
         int local = 0;
-        for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++local) {
+        for (int item = blockIdx.x; item < items; item += gridDim.x, ++local) {
+            const int tile = item / splits, sp = item % splits;
             const int buf = local & 1;
             const int64_t m0 = (int64_t)(tile / n_tiles) * kBM, n0 = (int64_t)(tile % n_tiles) * BN;
+            const int64_t row = m0 + q * 32 + lane;
+            const bool row_ok = row < m_eff;
+            const int64_t orow = (KIND == EPI_OUT_PROJ || KIND == EPI_SCATTER) && row_ok && splits == 1
+                                     ? out_row(epi, row) : row;
+            // the epilogue's global operands (residual rows, bias) do not depend on the
+            // accumulator: they are requested before waiting for it, so their latency
+            // overlaps the tile's MMAs
+            uint4 pre[kChunks][2];
+#pragma unroll
+            for (int i = 0; i < kChunks; ++i) {
+                const int c = 16 * (part + i * kParts);
+                pre[i][0] = pre[i][1] = make_uint4(0, 0, 0, 0);
+                if (row_ok && c < BN && splits == 1) {
+                    pre[i][0] = epi_pre8<KIND>(epi, orow, n0 + c, N);
+                    pre[i][1] = epi_pre8<KIND>(epi, orow, n0 + c + 8, N);
+                }
+            }
             const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&S.acc_full[buf]), (local >> 1) & 1));
             __syncwarp();                           // tcgen05.ld is .sync.aligned: whole warp, converged
             if (!ok) {
@@ -386,24 +415,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 break;
             }
             tc_fence_after();
-            const int64_t row = m0 + q * 32 + lane;
-            const bool row_ok = row < m_eff;
-            const int64_t orow = (KIND == EPI_OUT_PROJ || KIND == EPI_SCATTER) && row_ok ? out_row(epi, row) : row;
-#pragma unroll 1
-            for (int c = 16 * part; c < BN; c += 16 * kParts) {
-                // global reads first, so they are in flight while the accumulator is read
-                uint4 pre[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-                if (row_ok) {
-                    pre[0] = epi_pre8<KIND>(epi, orow, n0 + c, N);
-                    pre[1] = epi_pre8<KIND>(epi, orow, n0 + c + 8, N);
-                }
+#pragma unroll
+            for (int i = 0; i < kChunks; ++i) {
+                const int c = 16 * (part + i * kParts);           // warp-uniform
+                if (c >= BN) break;
                 float v[16];
                 tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kAccStride + c), v);
-                if (row_ok) {
+                if (splits > 1) {
+                    // this split's partial sums of the 16 columns, float32
+                    if (row_ok) {
+                        float* dst = partials + ((int64_t)sp * M + row) * N + n0 + c;
+                        if ((N & 3) == 0 && n0 + c + 16 <= N) {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                reinterpret_cast<float4*>(dst)[j] =
+                                    make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (n0 + c + j < N) dst[j] = v[j];
+                        }
+                    }
+                } else if (row_ok) {
 #pragma unroll
                     for (int g = 0; g < 2; ++g) {
                         const float (&v8)[8] = *reinterpret_cast<const float(*)[8]>(v + 8 * g);
-                        epi_fin8<KIND>(epi, row, orow, n0 + c + 8 * g, N, v8, pre[g]);
+                        epi_fin8<KIND>(epi, row, orow, n0 + c + 8 * g, N, v8, pre[i][g]);
                     }
                 }
             }
@@ -504,6 +541,22 @@ static int make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols,
     return NT_OK;
 }
 
+// Split-K: out = epilogue(sum over the splits' float32 partial sums), the sum in
+// split order.
+template <int KIND>
+__global__ void __launch_bounds__(256) gemm_splitk_epi_kernel(int64_t M, int64_t N, const int* m_count, int splits,
+                                                              const float* part, EpiArgs epi) {
+    const int64_t m_eff = m_count ? (int64_t)*m_count : M;
+    const int64_t total = m_eff * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / N, col = i % N;
+        float acc = part[row * N + col];
+        for (int s = 1; s < splits; ++s) acc += part[((int64_t)s * M + row) * N + col];
+        epi_apply<NT_BF16, KIND>(epi, row, col, acc);
+    }
+}
+
 template <int KIND, int BN>
 static int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     constexpr int STAGES = TcStages<BN>::value;
@@ -520,9 +573,21 @@ static int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t tiles = ((g.M + kBM - 1) / kBM) * ((g.N + BN - 1) / BN);
-    const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
-    kern<<<grid, kTcThreads, smem, stream>>>(ma, mb, g.M, g.N, g.K, g.m_count, g.epi, device_error_word(dev));
-    return check_launch("gemm_tc_kernel");
+    int splits = 1;
+    if (g.part) {
+        splits = gemm_split_k(g.M, g.N, g.K);
+        if ((int64_t)splits * g.M * g.N > g.part_elems) splits = 1;
+    }
+    const int64_t items = tiles * splits;
+    const unsigned grid = (unsigned)(items < sms ? items : sms);
+    kern<<<grid, kTcThreads, smem, stream>>>(ma, mb, g.M, g.N, g.K, g.m_count, g.epi, device_error_word(dev), splits,
+                                             g.part);
+    int rc2 = check_launch("gemm_tc_kernel");
+    if (rc2 != NT_OK || splits == 1) return rc2;
+    const int64_t blocks = std::min<int64_t>((g.M * g.N + 255) / 256, (int64_t)sms * 8);
+    gemm_splitk_epi_kernel<KIND><<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
+        g.M, g.N, g.m_count, splits, g.part, g.epi);
+    return check_launch("gemm_splitk_epi_kernel");
 }
 
 #ifndef NT_GEMM_TILE_OVERHEAD
@@ -553,6 +618,23 @@ static int pick_bn(int64_t M, int64_t N, int sms) {
         if (best_cost < 0 || cost < best_cost) { best = bn; best_cost = cost; }
     }
     return best;
+}
+
+#ifndef NT_GEMM_MAX_SPLITS
+#define NT_GEMM_MAX_SPLITS 8
+#endif
+// Fewer output tiles than SMs: split K so that about one work item runs per
+// SM, keeping at least 8 k-blocks (512 of K) per split for the TMA ring.
+int gemm_split_k(int64_t M, int64_t N, int64_t K) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int bn = pick_bn(M, N, sms);
+    const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+    const int64_t nk = (K + kBK - 1) / kBK;
+    int64_t s = tiles > 0 ? sms / tiles : 1;
+    s = std::min<int64_t>(s, nk / 8);
+    s = std::min<int64_t>(s, NT_GEMM_MAX_SPLITS);
+    return (int)std::max<int64_t>(s, 1);
 }
 
 template <int KIND>

@@ -127,7 +127,14 @@ struct GemmArgs {
     const void* Bw; int64_t ldb;  // [N,K] row-major
     const int* m_count;           // optional device row count (rows >= *m_count are skipped)
     EpiArgs epi;
+    // optional float32 scratch for split-K partial sums ([splits][M][N]); a GEMM
+    // with fewer output tiles than SMs splits K when it fits (gemm_split_k)
+    float* part;
+    int64_t part_elems;
 };
 int launch_gemm(int dtype, const GemmArgs& g, cudaStream_t stream);
+// K splits a bf16 GEMM of this shape takes on the current device when given
+// partial-sum scratch (1 = none); the scratch it needs is splits * M * N floats.
+int gemm_split_k(int64_t M, int64_t N, int64_t K);
 
 }  // namespace nt

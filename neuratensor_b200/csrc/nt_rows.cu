@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(int64_t M, int64_t D, cons
         T* yr = y + r * D;
         float ss = 0.f;
         if (vec) {
+            // unrolled so that several 16-byte loads of the row are in flight at once
+#pragma unroll 4
             for (int64_t i = (int64_t)lane * EPV; i < D; i += 32 * EPV) {
                 float v[EPV];
                 widen(xr + i, v);
@@ -68,6 +70,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(int64_t M, int64_t D, cons
         const float mean = ss / (float)D;
         const float rs = 1.0f / sqrtf(mean + 1.1920928955078125e-07f);
         if (vec) {
+#pragma unroll 4
             for (int64_t i = (int64_t)lane * EPV; i < D; i += 32 * EPV) {
                 float v[EPV], g[EPV];
                 widen(xr + i, v);

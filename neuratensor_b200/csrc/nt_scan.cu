@@ -910,9 +910,216 @@ ssm_step_kernel(ScanArgs a) {
     }
 }
 
+// The same step for many rows: one CTA per group of CPS channels walks a
+// range of rows (decode with many streams).  A channel's set-up -- log_A, the
+// HiPPO test, the general path's constants, D -- is done once for all its
+// rows instead of once per (row, channel), and a thread reads its own B/C
+// slice of each row (the CTA's channels share them through L1), so the row
+// loop has no barrier.  Per (row, channel, state) the arithmetic is the one of
+// ssm_step_kernel above, so both give the same results.
+template <int DT, int SDT, int TPC>
+__global__ void __launch_bounds__(kStepThreads, 4)
+ssm_step_rows_kernel(ScanArgs a, int rows_per_cta) {
+    using E = Elem<DT>;
+    using T = typename E::T;
+    using ST = typename Elem<SDT>::T;
+    constexpr int NPT = 8, NPR = 4, NP = TPC * NPT, CPS = kStepThreads / TPC;
+    const int tid = threadIdx.x, cl = tid / TPC, sub = tid % TPC, lane = tid & 31;
+    const unsigned gmask = TPC >= 32 ? 0xffffffffu : (((1u << TPC) - 1u) << (lane & ~(TPC - 1)));
+    const int64_t c = (int64_t)blockIdx.x * CPS + cl;
+    const int64_t d = a.d, N = a.N, Tl = a.T;
+    const int64_t b0 = (int64_t)blockIdx.y * rows_per_cta;
+    const int64_t b1 = b0 + rows_per_cta < a.B ? b0 + rows_per_cta : a.B;
+    const bool live = c < d;
+    const int64_t ld_bc = a.ld_bc > 0 ? a.ld_bc : N;
+    const T* logA = static_cast<const T*>(a.log_A) + (live ? c : 0) * N;
+    __shared__ float s_lnp1[NP];
+    for (int i = tid; i < NP; i += kStepThreads) s_lnp1[i] = logf((float)(i + 1));
+    __syncthreads();
+    const float la0 = live ? E::load(logA) : 0.f;
+    const float Abase = live ? -E::rnd(expf(la0)) : -1.f;
+    float2 A2v[NPR], civ[NPR], lmv[NPR];
+    float rn[NPT];                                   // 1/(n+1): B enters the HiPPO update as B/(n+1)
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < NPT; ++j) {
+        const int64_t n = (int64_t)sub * NPT + j;
+        const bool on = live && n < N;
+        rn[j] = 1.0f / (float)(n + 1);
+        if (on) {
+            const float la = E::load(logA + n);
+            if (DT == NT_BF16) {
+                if (!hippo_state_bf16(la, la0, s_lnp1[n])) ok = false;
+                if (la <= kLimLogA && fabsf(E::rnd(expf(la))) < 1e-6f) ok = false;
+            } else {
+                const float A = -E::rnd(expf(la));
+                if (fabsf(A - (float)(n + 1) * Abase) > 1e-6f * fabsf(A) || fabsf(A) < 1e-6f) ok = false;
+            }
+        }
+    }
+    const unsigned okm = __ballot_sync(0xffffffffu, ok);
+    const bool hippo = (okm & gmask) == gmask;
+    if (!hippo) {
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) {
+            const int64_t n = (int64_t)sub * NPT + j;
+            const bool on = live && n < N;
+            const float A = on ? -E::rnd(expf(E::load(logA + n))) : 0.f;
+            const bool lim = on && fabsf(A) < 1e-6f;
+            const float np1 = (float)(n + 1);
+            const float ci = (lim || A == 0.f) ? 0.f : np1 / A;
+            if (j & 1) { A2v[j / 2].y = A * kLog2e; civ[j / 2].y = ci; lmv[j / 2].y = lim ? np1 : 0.f; }
+            else { A2v[j / 2].x = A * kLog2e; civ[j / 2].x = ci; lmv[j / 2].x = lim ? np1 : 0.f; }
+        }
+    }
+    const float a0l = Abase * kLog2e, ra0 = 1.0f / Abase;
+    const float np1a = (float)(sub * NPT + 1), np1b = (float)(sub * NPT + 2);
+    const float Dv = live ? E::load(static_cast<const T*>(a.D) + c) : 0.f;
+    const bool sparse_rows = a.row_pos != nullptr && a.sparse_flag != nullptr && *a.sparse_flag != 0;
+    const bool full_slice = live && (int64_t)(sub + 1) * NPT <= N;
+    // 16-byte B/C slice loads when every row's slice starts 16-byte aligned
+    const bool vec_bc = full_slice && sizeof(T) == 2 && ld_bc % 8 == 0 &&
+                        ((reinterpret_cast<uintptr_t>(a.Bm) | reinterpret_cast<uintptr_t>(a.Cm)) & 15) == 0;
+    const T* p_u = static_cast<const T*>(a.u);
+    const T* p_dt = static_cast<const T*>(a.dt);
+    const T* p_B = static_cast<const T*>(a.Bm);
+    const T* p_C = static_cast<const T*>(a.Cm);
+    const T* p_g = static_cast<const T*>(a.gate);
+    auto slice = [&](const T* p, int64_t row, float (&v)[NPT]) {
+        const T* q = p + row * ld_bc + sub * NPT;
+        if (vec_bc) {
+            const uint4 w = *reinterpret_cast<const uint4*>(q);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[2 * i] = __uint_as_float(ww[i] << 16);
+                v[2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) v[j] = (live && (int64_t)sub * NPT + j < N) ? E::to_f(q[j]) : 0.f;
+        }
+    };
+    for (int64_t bi = b0; bi < b1; ++bi) {
+        float hs[NPT];
+#pragma unroll
+        for (int j = 0; j < NPT; ++j) hs[j] = 0.f;
+        if (a.state_in && full_slice) {
+            load_state8(static_cast<const ST*>(a.state_in) + (bi * d + c) * N + sub * NPT, hs);
+        } else if (a.state_in && live) {
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) {
+                const int64_t n = (int64_t)sub * NPT + j;
+                if (n >= N) continue;
+                const int64_t si = (bi * d + c) * N + n;
+                hs[j] = SDT == NT_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.state_in)[si])
+                                       : static_cast<const float*>(a.state_in)[si];
+            }
+        }
+        float2 hv[NPR];
+#pragma unroll
+        for (int j = 0; j < NPR; ++j) hv[j] = make_float2(hs[2 * j], hs[2 * j + 1]);
+        for (int64_t t = 0; t < Tl; ++t) {
+            const int64_t row = bi * Tl + t;
+            float Bv[NPT], Cv[NPT];
+            slice(p_B, row, Bv);
+            slice(p_C, row, Cv);
+            const float u = live ? E::to_f(p_u[row * d + c]) : 0.f;
+            const float dtv = live ? E::to_f(p_dt[row * d + c]) : 0.f;
+            float2 Bp[NPR], Cp[NPR], av[NPR];
+#pragma unroll
+            for (int j = 0; j < NPR; ++j) {
+                Bp[j] = make_float2(Bv[2 * j] * rn[2 * j], Bv[2 * j + 1] * rn[2 * j + 1]);
+                Cp[j] = make_float2(Cv[2 * j], Cv[2 * j + 1]);
+            }
+            if (hippo) {
+                const float x0 = dtv * a0l, s = u * ra0;
+                const float q = ex2(x0);
+                const float qs = q * q, qm = __fmaf_rn(q, q, -1.0f);
+                av[0] = make_float2(ex2(x0 * np1a) - 1.0f, ex2(x0 * np1b) - 1.0f);
+                const float2 qq = make_float2(qs, qs), qqm = make_float2(qm, qm), ss = make_float2(s, s);
+#pragma unroll
+                for (int j = 1; j < NPR; ++j) av[j] = pfma(av[j - 1], qq, qqm);
+#pragma unroll
+                for (int j = 0; j < NPR; ++j) hv[j] = pfma(av[j], pfma(Bp[j], ss, hv[j]), hv[j]);
+            } else {
+                const float2 uu = make_float2(u, u), dd = make_float2(dtv, dtv);
+#pragma unroll
+                for (int j = 0; j < NPR; ++j) {
+                    av[j] = make_float2(ex2(dtv * A2v[j].x), ex2(dtv * A2v[j].y));
+                    const float2 coef = pfma(dd, lmv[j], pfma(av[j], civ[j], make_float2(-civ[j].x, -civ[j].y)));
+                    const float2 bu = pmul(coef, pmul(Bp[j], uu));
+                    hv[j] = pfma(av[j], hv[j], bu);
+                }
+            }
+            float2 ya = pmul(Cp[0], hv[0]), yb = pmul(Cp[1], hv[1]);
+            ya = pfma(Cp[2], hv[2], ya);
+            yb = pfma(Cp[3], hv[3], yb);
+            float y = (ya.x + yb.x) + (ya.y + yb.y);
+#pragma unroll
+            for (int half = TPC / 2; half >= 1; half >>= 1) y += __shfl_xor_sync(gmask, y, half);
+            if (sub == 0 && live) {
+                const float yv = __fadd_rn(y, __fmul_rn(Dv, u));
+                float o = E::rnd(yv);
+                if (p_g) {
+                    const float gv = E::to_f(p_g[row * d + c]);
+                    o = E::rnd(o * (a.gate_is_silu ? gv : E::rnd(silu_f(gv))));
+                }
+                int64_t orow = row;
+                if (sparse_rows) orow = a.row_pos[row];
+                if (orow >= 0) static_cast<T*>(a.y)[orow * d + c] = E::from_f(o);
+            }
+        }
+        if (a.state_out && live) {
+            float ho[NPT];
+#pragma unroll
+            for (int j = 0; j < NPT; ++j) ho[j] = (j & 1) ? hv[j / 2].y : hv[j / 2].x;
+            if (full_slice) {
+                store_state8(static_cast<ST*>(a.state_out) + (bi * d + c) * N + sub * NPT, ho);
+            } else {
+#pragma unroll
+                for (int j = 0; j < NPT; ++j) {
+                    const int64_t n = (int64_t)sub * NPT + j;
+                    if (n >= N) continue;
+                    const int64_t si = (bi * d + c) * N + n;
+                    if (SDT == NT_BF16) static_cast<__nv_bfloat16*>(a.state_out)[si] = __float2bfloat16_rn(ho[j]);
+                    else static_cast<float*>(a.state_out)[si] = ho[j];
+                }
+            }
+        }
+    }
+}
+
+#ifndef NT_STEP_ROWS_MIN_B
+#define NT_STEP_ROWS_MIN_B 16
+#endif
 template <int DT, int SDT>
 int launch_step(const ScanArgs& a, cudaStream_t stream) {
     const int tpc = pow2_at_least((a.N + 7) / 8);
+    if (a.B >= NT_STEP_ROWS_MIN_B) {
+        // many rows: channel groups walk row ranges, about four CTAs per SM in all
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int64_t groups = (a.d + kStepThreads / tpc - 1) / (kStepThreads / tpc);
+        int64_t rg = (4LL * sms + groups - 1) / groups;
+        rg = rg < 1 ? 1 : (rg > a.B ? a.B : rg);
+        const int rows = (int)((a.B + rg - 1) / rg);
+        rg = (a.B + rows - 1) / rows;
+        auto go = [&](auto kern) {
+            kern<<<dim3((unsigned)groups, (unsigned)rg), kStepThreads, 0, stream>>>(a, rows);
+        };
+        switch (tpc) {
+            case 1: go(ssm_step_rows_kernel<DT, SDT, 1>); break;
+            case 2: go(ssm_step_rows_kernel<DT, SDT, 2>); break;
+            case 4: go(ssm_step_rows_kernel<DT, SDT, 4>); break;
+            case 8: go(ssm_step_rows_kernel<DT, SDT, 8>); break;
+            case 16: go(ssm_step_rows_kernel<DT, SDT, 16>); break;
+            case 32: go(ssm_step_rows_kernel<DT, SDT, 32>); break;
+            default: return fail(NT_ERR_ARG, "scan: d_state %lld > 256 unsupported", (long long)a.N);
+        }
+        return check_launch("ssm_step_rows_kernel");
+    }
     auto go = [&](auto kern, int tpc_) {
         dim3 grid((unsigned)((a.d + kStepThreads / tpc_ - 1) / (kStepThreads / tpc_)), (unsigned)a.B);
         kern<<<grid, kStepThreads, 0, stream>>>(a);

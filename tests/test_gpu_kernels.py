@@ -166,6 +166,38 @@ def test_selective_scan_short_sequences_vs_oracle(nat, Nst, hippo):
         np.testing.assert_allclose(N(so), rs, rtol=1e-4, atol=1e-6)
 
 
+@pytest.mark.parametrize("Nst", [12, 32, 128])
+@pytest.mark.parametrize("hippo", [True, False])
+def test_selective_scan_many_row_steps_match_per_row_kernel(nat, Nst, hippo):
+    """T <= 4 with 16 or more rows runs the row-walking step kernel (one CTA per
+    channel group over a range of rows); fewer rows run the per-(row, channel)
+    one.  Both take the same arithmetic, so 40 rows in one call equal the same
+    rows in calls of 8, bit for bit (fp32, and bf16 with bf16 state and a gate),
+    and match the oracle."""
+    rng = np.random.default_rng(Nst + 7 * hippo)
+    B = 40
+    for Tn in (1, 3):
+        u, dt, Bm, Cm, log_A, D, st = _scan_inputs(rng, B, Tn, 200, Nst, hippo=hippo, limit=not hippo)
+        args = [T(a) for a in (u, dt, Bm, Cm)]
+        y, so = nat.selective_scan(*args, T(log_A), T(D), T(st))
+        ys, ss = [], []
+        for r in range(0, B, 8):
+            yr, sr = nat.selective_scan(*(a[r:r + 8] for a in args), T(log_A), T(D), T(st[r:r + 8]))
+            ys.append(yr)
+            ss.append(sr)
+        assert torch.equal(y, torch.cat(ys)) and torch.equal(so, torch.cat(ss))
+        ry, rs = O.ssm_scan(u, dt, Bm, Cm, log_A, D, st, "fp32")
+        np.testing.assert_allclose(N(y), ry, rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(N(so), rs, rtol=1e-4, atol=1e-6)
+        bf = torch.bfloat16
+        g = T(rng.normal(0, 1, u.shape).astype(np.float32), bf)
+        ab = [a.to(bf) for a in args]
+        yb, sb = nat.selective_scan(*ab, T(log_A, bf), T(D, bf), T(st, bf), gate=g, state_dtype=bf)
+        yp = [nat.selective_scan(*(a[r:r + 8] for a in ab), T(log_A, bf), T(D, bf), T(st[r:r + 8], bf),
+                                 gate=g[r:r + 8], state_dtype=bf) for r in range(0, B, 8)]
+        assert torch.equal(yb, torch.cat([p[0] for p in yp])) and torch.equal(sb, torch.cat([p[1] for p in yp]))
+
+
 def test_selective_scan_steps_chain_like_one_call(nat):
     """16 calls of 4 steps with carried state (step kernel) == one 64-step call
     (chunked kernel), fp32 and bf16 gated with bf16 state."""
